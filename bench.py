@@ -1,0 +1,430 @@
+"""Benchmark of the paged KV-cache decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama2_7b_ragged_decode] [--v1-split on|off]
+
+A step is one decode step of the workload over resident HBM inputs:
+reshape_and_cache of the new tokens, then paged attention (v1 for contexts
+<= 8192 tokens, else v2 + reduce), plus copy_blocks for workloads with COW
+forks.  The metric is KV bytes read per step (each (token, KV head) K and V
+row once) / step time, in GB/s, summed over ranks; tokens/s (decode rows per
+second per layer) is reported beside it.
+
+Multi-GPU (torchrun, one process per GPU): every rank owns its own block pool
+and batch (weak scaling: the same workload shape per GPU, seeded per rank);
+no collective touches the data path.  Timing is CUDA events on the launching
+stream, max over ranks.
+
+--impl reference runs CacheFlow's own CPU decode step (oracle/_ref, built
+from the reference sources) on a bounded sample of the same workload on the
+host cores; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from cacheflow_b200 import workloads  # noqa: E402
+
+METRIC = "Paged decode attn: HBM GB/s (% of peak), tokens/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+DTYPE_NAME = {"f32": "f32", "f16": "f16", "bf16": "bf16"}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (nvidia-smi, 100 ms period).
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons, loaded = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                clk, cmax, util = float(f[1]), float(f[2]), float(f[3])
+            except ValueError:
+                continue
+            mx = cmax
+            sm.append(clk)
+            if util > 0:
+                loaded.append(clk)
+            for n, v in zip(names, f[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        use = loaded or sm
+        return {"sm_mhz": statistics.median(use) if use else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(loaded)}
+
+
+# ---------------------------------------------------------------------------
+# Our arm.
+# ---------------------------------------------------------------------------
+def fill_normal_(t, std, gen):
+    return t.normal_(0.0, std, generator=gen)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from cacheflow_b200 import _lib, ops
+    from cacheflow_b200.engine import DecodeEngine
+
+    rank, world, local = dist_env()
+    _lib.load()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    w = workloads.make(args.workload, seed=1234 + rank)
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[w.dtype]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    S, H, Hkv, D = w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim
+    k_cache = torch.empty(w.cache_shape(), dtype=tdt, device=dev)
+    v_cache = torch.empty_like(k_cache)
+    fill_normal_(k_cache, w.std, gen)
+    fill_normal_(v_cache, w.std, gen)
+    T = len(w.slot_mapping)
+    q = torch.empty((S, H, D), dtype=tdt, device=dev).normal_(0, w.std, generator=gen)
+    k_new = torch.empty((T, Hkv, D), dtype=tdt, device=dev).normal_(0, w.std, generator=gen)
+    v_new = torch.empty_like(k_new).normal_(0, w.std, generator=gen)
+    slots = torch.from_numpy(w.slot_mapping).to(dev)
+    tables = torch.from_numpy(w.block_tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    pairs = torch.from_numpy(w.copy_pairs).to(dev) if len(w.copy_pairs) else None
+    mctx = w.max_context_len
+
+    engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"))
+    engine.q[:S].copy_(q)
+    engine.tables.copy_(tables)
+    engine.ctx.copy_(ctx)
+    stream = engine.stream
+
+    att_ev = []
+
+    def step(record=False):
+        if pairs is not None:
+            ops.copy_blocks(k_cache, v_cache, pairs)
+        ops.reshape_and_cache(k_new, v_new, k_cache, v_cache, slots)
+        if record:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            engine.attend(S, mctx)
+            b.record(stream)
+            att_ev.append((a, b))
+        else:
+            engine.attend(S, mctx)
+
+    launches_per_step = None
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        launches_per_step = engine.launches_per_step + 1 + (1 if pairs is not None else 0)
+        torch.cuda.synchronize(dev)
+        if ops.device_errors(local) != 0:
+            raise RuntimeError("device error word set during warm-up")
+        if world > 1:
+            dist.barrier()
+        clocks = ClockSampler(local) if rank == 0 else None
+        if clocks:
+            clocks.start()
+            time.sleep(0.25)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(record=True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        clock_info = clocks.stop() if clocks else None
+    ms_step = t0.elapsed_time(t1) / args.steps
+    att_ms = sum(a.elapsed_time(b) for a, b in att_ev) / len(att_ev)
+
+    # e2e through the public engine API with pinned host buffers.
+    pin = dict(
+        q=q.cpu().pin_memory(), k=k_new.cpu().pin_memory(), v=v_new.cpu().pin_memory(),
+        s=slots.cpu().pin_memory(), t=tables.cpu().pin_memory(), c=ctx.cpu().pin_memory(),
+        o=torch.empty((S, H, D), dtype=tdt).pin_memory())
+    for _ in range(max(3, args.warmup // 4)):
+        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_steps = max(1, args.steps // 2)
+    for _ in range(e2e_steps):
+        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if ops.device_errors(local) != 0:
+        raise RuntimeError("device error word set during the timed region")
+
+    times = torch.tensor([ms_step, att_ms, e2e_ms], dtype=torch.float64, device=dev)
+    totals = torch.tensor([w.kv_bytes(), S], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.all_reduce(totals, op=dist.ReduceOp.SUM)
+    ms_step, att_ms, e2e_ms = times.tolist()
+    kv_total, seqs_total = totals.tolist()
+
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        alg_bytes = w.kv_bytes() + w.qo_bytes() + w.table_bytes()
+        achieved = alg_bytes / (att_ms * 1e-3) / 1e9
+        value = kv_total / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": DTYPE_NAME[w.dtype],
+            "data": "synthetic (seeded N(0,%g) caches, shapes of the workload)" % w.std,
+            "config": {
+                "workload": w.name,
+                "num_seqs_per_gpu": S,
+                "num_heads": H,
+                "num_kv_heads": Hkv,
+                "head_dim": D,
+                "block_size": 16,
+                "context_lens": "min %d / mean %.0f / max %d" % (w.context_lens.min(), w.context_lens.mean(),
+                                                                  w.context_lens.max()),
+                "pool_blocks_per_gpu": w.num_blocks,
+                "kv_bytes_per_step_per_gpu": w.kv_bytes(),
+                "attention": "v1" if mctx <= 8192 else "v2",
+                "v1_split": args.v1_split,
+                "l2": "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (w.kv_bytes() / 1e9),
+                "parallelism": f"dp{world} (sequence-sharded pools, no data-path collective)",
+            },
+            "tokens_per_s": round(seqs_total / (ms_step * 1e-3), 1),
+            "frac_of_hbm_peak": round(value / (peak * world), 4),
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "paged_attention" + ("_v1" if mctx <= 8192 else "_v2+reduce"),
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": peak_kind,
+                "alg_bytes_per_launch": alg_bytes,
+                "kernel_ms": round(att_ms, 4),
+                "traffic": traffic_from_profiles(w.name),
+            },
+            "e2e": {
+                "value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 1),
+                "unit": UNIT,
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": engine.h2d_bytes(S, T),
+                "d2h_bytes_per_step": engine.d2h_bytes(S),
+                "api": "cacheflow_b200.engine.DecodeEngine.step (pinned host in, pinned host out)",
+            },
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock_info,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def traffic_from_profiles(workload: str):
+    """DRAM bytes per launch of the attention kernel from a committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"traffic_{workload}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CacheFlow's own CPU decode step on a bounded sample (reference arm / baseline).
+# ---------------------------------------------------------------------------
+def reference_sample(w: workloads.Workload, max_seqs: int):
+    """The first `max_seqs` rows of the workload with their blocks renumbered
+    into a compact fp32 pool (the reference is fp32-only)."""
+    rows = np.arange(min(max_seqs, w.num_seqs))
+    ctx = w.context_lens[rows]
+    nblk = (ctx.astype(np.int64) + 15) // 16
+    tables = np.zeros((len(rows), int(nblk.max())), np.int32)
+    remap = {}
+    for i, r in enumerate(rows):
+        for b in range(nblk[i]):
+            old = int(w.block_tables[r, b])
+            tables[i, b] = remap.setdefault(old, len(remap))
+    return ctx, tables, len(remap)
+
+
+def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | None = None, warmup: int = 1):
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    n = min(w.num_seqs, 16)
+    ctx, tables, pool = reference_sample(w, n)
+    ref = oracle.RefCpu(w.num_heads, w.num_kv_heads, w.head_dim, pool, threads)
+    try:
+        k, v = ref.caches()
+        rng = np.random.default_rng(7)
+        k[...] = rng.standard_normal(k.shape, dtype=np.float32) * np.float32(w.std)
+        v[...] = rng.standard_normal(v.shape, dtype=np.float32) * np.float32(w.std)
+        ref.set_batch(ctx, tables)
+        for _ in range(warmup):
+            ref.step()
+        times = []
+        t_start = time.perf_counter()
+        while True:
+            times.append(ref.step())
+            if steps is not None:
+                if len(times) >= steps:
+                    break
+            elif time.perf_counter() - t_start > budget_s:
+                break
+    finally:
+        ref.close()
+    t = sum(times) / len(times)
+    sample_bytes = int(ctx.astype(np.int64).sum()) * 2 * w.num_kv_heads * w.head_dim * w.elem_bytes
+    return {
+        "value": round(sample_bytes / t / 1e9, 3),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "reference",
+        "sample": (f"CacheFlow BatchDecodeEngine::step, CPU build (batch_decode.cpp:33-88,190-240; fp32, "
+                   f"reads K only, no output) on the first {len(ctx)} of {w.num_seqs} sequences of {w.name} "
+                   f"({int(ctx.sum())} tokens), {len(times)} steps of {t*1e3:.1f} ms, {threads} threads; "
+                   f"value = that sample's {w.dtype} KV bytes / step time"),
+        "tokens_per_s": round(len(ctx) / t, 2),
+    }
+
+
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    w = workloads.make(args.workload, seed=1234)
+    cb = cpu_baseline(w, steps=args.steps, warmup=args.warmup)
+    ms = cb["sample"]
+    line = {
+        "metric": METRIC,
+        "value": cb["value"],
+        "unit": UNIT,
+        "impl": "reference",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,%g))" % w.std,
+        "config": {"workload": w.name, "num_seqs_per_gpu": w.num_seqs, "num_heads": w.num_heads,
+                   "num_kv_heads": w.num_kv_heads, "head_dim": w.head_dim, "block_size": 16},
+        "tokens_per_s": cb["tokens_per_s"],
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="llama2_7b_ragged_decode", choices=sorted(workloads.WORKLOADS))
+    ap.add_argument("--v1-split", choices=["on", "off"], default="on")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,273 @@
+// cache_ops.cu -- KV-cache data movement for sm_100a: reshape_and_cache,
+// block-pair copies (copy_blocks, swap_blocks, compact_kv_cache) and
+// memset_blocks.
+//
+// All of these are pure byte movement and HBM-bound (or host-link-bound for
+// swaps), so the kernels move 16-byte vectors with 64-bit offsets, spread
+// every block over many CTAs, and range-check each device-side index
+// (skip + record in the error word, never trap).
+//
+// Reference semantics followed (CacheFlow src/cacheflow/cuda/):
+//   reshape_and_cache_kernel  kv_cache_kernels.cu:17-44  (slot math :34-40)
+//   copy_blocks_kernel        kv_cache_kernels.cu:63-84  (pair layout :71-73)
+//   swap_blocks_kernel        kv_cache_kernels.cu:105-131 (launcher :121-131)
+//   compact_kv_cache_kernel   kv_cache_kernels.cu:140-183 (src == dst skipped :152)
+//   memset_blocks_kernel      memory_utils.cu:46-69
+#include "cf_device.cuh"
+#include "cf_internal.h"
+
+namespace cfb {
+
+__device__ uint32_t g_cache_errors;
+
+__device__ __forceinline__ void cache_error(uint32_t bits) { atomicOr(&g_cache_errors, bits); }
+
+// ---------------------------------------------------------------------------
+// reshape_and_cache: one thread per 16-byte vector of a (token, kv head) row;
+// K and V share the slot lookup.  Rows are written whole and contiguous.
+// ---------------------------------------------------------------------------
+template <typename V>
+__global__ void __launch_bounds__(256)
+    reshape_and_cache_kernel(const V* __restrict__ key, const V* __restrict__ value,
+                             V* __restrict__ key_cache, V* __restrict__ value_cache,
+                             const int32_t* __restrict__ slot_mapping, int64_t num_rows,
+                             int32_t num_kv_heads, int32_t vecs_per_row, int32_t block_size,
+                             int64_t num_slots) {
+  const int64_t total = num_rows * vecs_per_row;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = g / vecs_per_row;
+    const int32_t v = (int32_t)(g - row * vecs_per_row);
+    const int64_t tok = row / num_kv_heads;
+    const int32_t head = (int32_t)(row - tok * num_kv_heads);
+    const int64_t slot = slot_mapping[tok];
+    if (slot < 0) continue;  // padding token
+    if (slot >= num_slots) {
+      if (v == 0) cache_error(CF_DEVERR_SLOT);
+      continue;
+    }
+    const int64_t blk = slot / block_size;
+    const int64_t off = slot - blk * block_size;
+    const int64_t dst_row = (blk * num_kv_heads + head) * block_size + off;
+    key_cache[dst_row * vecs_per_row + v] = key[g];
+    value_cache[dst_row * vecs_per_row + v] = value[g];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block-pair copy.  Up to two (src base, dst base) streams share one list of
+// (src id, dst id) pairs: copy_blocks uses (K,K) and (V,V) within one pool,
+// swap_blocks uses one (src pool, dst pool) stream, compact uses (K,K),(V,V)
+// with separate id arrays.  grid = (chunks per block, pairs).
+// ---------------------------------------------------------------------------
+struct PairStreams {
+  const uint8_t* src[2];
+  uint8_t* dst[2];
+  int32_t count;
+};
+
+template <typename IdT>
+struct PairIds {
+  const IdT* src;  // src id of pair i at src[i * stride]
+  const IdT* dst;
+  int32_t stride;
+};
+
+constexpr int kCopyThreads = 256;
+constexpr int kCopyUnroll = 4;  // 16-byte vectors per thread per stream
+
+template <typename V, typename IdT, bool kSkipSame>
+__global__ void __launch_bounds__(kCopyThreads)
+    pair_copy_kernel(PairStreams st, PairIds<IdT> ids, int32_t num_pairs, int64_t vecs_per_block,
+                     int64_t num_src_blocks, int64_t num_dst_blocks) {
+  for (int64_t pair = blockIdx.y; pair < num_pairs; pair += gridDim.y) {
+    const int64_t s = (int64_t)ids.src[pair * ids.stride];
+    const int64_t d = (int64_t)ids.dst[pair * ids.stride];
+    if (s < 0 || s >= num_src_blocks || d < 0 || d >= num_dst_blocks) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) cache_error(CF_DEVERR_BLOCK_ID);
+      continue;
+    }
+    if (kSkipSame && s == d) continue;
+    const int64_t base = (int64_t)blockIdx.x * kCopyThreads * kCopyUnroll + threadIdx.x;
+    for (int k = 0; k < st.count; ++k) {
+      const V* src = reinterpret_cast<const V*>(st.src[k]) + s * vecs_per_block;
+      V* dst = reinterpret_cast<V*>(st.dst[k]) + d * vecs_per_block;
+      V tmp[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + (int64_t)u * kCopyThreads;
+        if (i < vecs_per_block) tmp[u] = src[i];
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + (int64_t)u * kCopyThreads;
+        if (i < vecs_per_block) dst[i] = tmp[u];
+      }
+    }
+  }
+}
+
+template <typename V>
+__global__ void __launch_bounds__(kCopyThreads)
+    memset_blocks_kernel(uint8_t* cache, const int32_t* __restrict__ ids, int32_t num_listed,
+                         int64_t vecs_per_block, int64_t num_blocks) {
+  for (int64_t i = blockIdx.y; i < num_listed; i += gridDim.y) {
+    const int64_t b = ids[i];
+    if (b < 0 || b >= num_blocks) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) cache_error(CF_DEVERR_BLOCK_ID);
+      continue;
+    }
+    V* dst = reinterpret_cast<V*>(cache) + b * vecs_per_block;
+    const int64_t base = (int64_t)blockIdx.x * kCopyThreads * kCopyUnroll + threadIdx.x;
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+      const int64_t j = base + (int64_t)u * kCopyThreads;
+      if (j < vecs_per_block) dst[j] = V{};
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers.
+// ---------------------------------------------------------------------------
+namespace {
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// Widest vector (16, 4 or 1 bytes) that every pointer and the block size allow.
+int vector_bytes(std::initializer_list<const void*> ptrs, int64_t bytes) {
+  int w = 16;
+  for (const void* p : ptrs) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    while (w > 1 && (a % w) != 0) w /= 4;
+  }
+  while (w > 1 && (bytes % w) != 0) w /= 4;
+  return w < 4 ? 1 : w;
+}
+
+template <typename IdT, bool kSkipSame>
+cf_status launch_pairs(const PairStreams& st, const PairIds<IdT>& ids, int32_t num_pairs,
+                       int64_t block_bytes, int64_t num_src, int64_t num_dst,
+                       cudaStream_t stream) {
+  if (num_pairs == 0) return CF_OK;
+  const int w = vector_bytes({st.src[0], st.dst[0], st.count > 1 ? st.src[1] : nullptr,
+                              st.count > 1 ? st.dst[1] : nullptr},
+                             block_bytes);
+  const int64_t vecs = block_bytes / w;
+  const int64_t per_cta = (int64_t)kCopyThreads * kCopyUnroll;
+  const int64_t chunks = (vecs + per_cta - 1) / per_cta;
+  if (chunks > 0x7fffffff) return CF_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)chunks, (unsigned)(num_pairs < 65535 ? num_pairs : 65535));
+  if (w == 16)
+    pair_copy_kernel<uint4, IdT, kSkipSame>
+        <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
+  else if (w == 4)
+    pair_copy_kernel<uint32_t, IdT, kSkipSame>
+        <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
+  else
+    pair_copy_kernel<uint8_t, IdT, kSkipSame>
+        <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
+  return check_launch();
+}
+
+}  // namespace
+
+cf_status launch_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                                   void* value_cache, const int32_t* slot_mapping,
+                                   int32_t num_tokens, int32_t num_kv_heads, int64_t row_bytes,
+                                   int32_t block_size, int64_t num_blocks, cudaStream_t stream) {
+  if (num_tokens == 0) return CF_OK;
+  const int w = vector_bytes({key, value, key_cache, value_cache}, row_bytes);
+  const int64_t rows = (int64_t)num_tokens * num_kv_heads;
+  const int64_t vpr = row_bytes / w;
+  const int64_t total = rows * vpr;
+  const int64_t want = (total + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const int64_t slots = num_blocks * block_size;
+  if (w == 16)
+    reshape_and_cache_kernel<uint4><<<grid, 256, 0, stream>>>(
+        (const uint4*)key, (const uint4*)value, (uint4*)key_cache, (uint4*)value_cache,
+        slot_mapping, rows, num_kv_heads, (int32_t)vpr, block_size, slots);
+  else if (w == 4)
+    reshape_and_cache_kernel<uint32_t><<<grid, 256, 0, stream>>>(
+        (const uint32_t*)key, (const uint32_t*)value, (uint32_t*)key_cache,
+        (uint32_t*)value_cache, slot_mapping, rows, num_kv_heads, (int32_t)vpr, block_size,
+        slots);
+  else
+    reshape_and_cache_kernel<uint8_t><<<grid, 256, 0, stream>>>(
+        (const uint8_t*)key, (const uint8_t*)value, (uint8_t*)key_cache, (uint8_t*)value_cache,
+        slot_mapping, rows, num_kv_heads, (int32_t)vpr, block_size, slots);
+  return check_launch();
+}
+
+cf_status launch_copy_pairs64(void* key_cache, void* value_cache, const int64_t* mapping,
+                              int32_t num_pairs, int64_t block_bytes, int64_t num_blocks,
+                              cudaStream_t stream) {
+  PairStreams st{{(const uint8_t*)key_cache, (const uint8_t*)value_cache},
+                 {(uint8_t*)key_cache, (uint8_t*)value_cache},
+                 2};
+  PairIds<int64_t> ids{mapping, mapping + 1, 2};
+  return launch_pairs<int64_t, false>(st, ids, num_pairs, block_bytes, num_blocks, num_blocks,
+                                      stream);
+}
+
+cf_status launch_swap_pairs64(const void* src_cache, void* dst_cache, const int64_t* mapping,
+                              int32_t num_pairs, int64_t block_bytes, cudaStream_t stream) {
+  PairStreams st{{(const uint8_t*)src_cache, nullptr}, {(uint8_t*)dst_cache, nullptr}, 1};
+  PairIds<int64_t> ids{mapping, mapping + 1, 2};
+  // Pool sizes are unknown to the reference interface: ids are checked >= 0 only.
+  const int64_t unchecked = INT64_MAX / (block_bytes > 0 ? block_bytes : 1);
+  return launch_pairs<int64_t, false>(st, ids, num_pairs, block_bytes, unchecked, unchecked,
+                                      stream);
+}
+
+cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t* src_ids,
+                               const int32_t* dst_ids, int32_t num_moves, int64_t block_bytes,
+                               int64_t num_blocks, cudaStream_t stream) {
+  PairStreams st{{(const uint8_t*)key_cache, (const uint8_t*)value_cache},
+                 {(uint8_t*)key_cache, (uint8_t*)value_cache},
+                 2};
+  PairIds<int32_t> ids{src_ids, dst_ids, 1};
+  return launch_pairs<int32_t, true>(st, ids, num_moves, block_bytes, num_blocks, num_blocks,
+                                     stream);
+}
+
+cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_listed,
+                               int64_t block_bytes, int64_t num_blocks, cudaStream_t stream) {
+  if (num_listed == 0) return CF_OK;
+  const int w = vector_bytes({cache}, block_bytes);
+  const int64_t vecs = block_bytes / w;
+  const int64_t per_cta = (int64_t)kCopyThreads * kCopyUnroll;
+  const int64_t chunks = (vecs + per_cta - 1) / per_cta;
+  if (chunks > 0x7fffffff) return CF_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)chunks, (unsigned)(num_listed < 65535 ? num_listed : 65535));
+  if (w == 16)
+    memset_blocks_kernel<uint4>
+        <<<grid, kCopyThreads, 0, stream>>>((uint8_t*)cache, ids, num_listed, vecs, num_blocks);
+  else if (w == 4)
+    memset_blocks_kernel<uint32_t>
+        <<<grid, kCopyThreads, 0, stream>>>((uint8_t*)cache, ids, num_listed, vecs, num_blocks);
+  else
+    memset_blocks_kernel<uint8_t>
+        <<<grid, kCopyThreads, 0, stream>>>((uint8_t*)cache, ids, num_listed, vecs, num_blocks);
+  return check_launch();
+}
+
+cf_status cache_ops_read_errors(uint32_t* bits, bool clear) {
+  uint32_t v = 0;
+  cf_status s = cuda_status(cudaMemcpyFromSymbol(&v, g_cache_errors, sizeof(v)));
+  if (s != CF_OK) return s;
+  *bits |= v;
+  if (clear) {
+    const uint32_t zero = 0;
+    s = cuda_status(cudaMemcpyToSymbol(g_cache_errors, &zero, sizeof(zero)));
+  }
+  return s;
+}
+
+}  // namespace cfb

@@ -1,0 +1,458 @@
+// capi.cu -- the library's C ABI (include/cacheflow_b200.h) and the C++
+// entry points with CacheFlow's exact signatures
+// (include/cacheflow_b200_compat.hpp).  Host code only: argument checks,
+// dispatch to the launchers, status / error-word plumbing, the copy-engine
+// swap path and the host-side compaction planner.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/cacheflow_b200.h"
+#include "../../include/cacheflow_b200_compat.hpp"
+#include "cf_internal.h"
+
+namespace cfb {
+
+namespace {
+thread_local int32_t t_last_cuda_error = 0;
+}
+
+cf_status cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return CF_OK;
+  t_last_cuda_error = (int32_t)err;
+  return CF_ERR_CUDA;
+}
+
+namespace {
+
+constexpr int32_t kV2PartitionTokens = 512;  // CacheFlow's PARTITION_SIZE (paged_attention.cu:368)
+
+// Tokens per partition of the split path of cf_paged_attention_v1; 0 disables
+// splitting.  CF_V1_SPLIT_TOKENS (a multiple of 16) overrides the default.
+int32_t v1_split_tokens() {
+  static int32_t v = [] {
+    int32_t d = 1024;
+    if (const char* e = std::getenv("CF_V1_SPLIT_TOKENS")) {
+      long x = std::strtol(e, nullptr, 10);
+      if (x >= 0 && x % 16 == 0 && x <= (1 << 24)) d = (int32_t)x;
+    }
+    return d;
+  }();
+  return v;
+}
+
+// Address under which the current device can dereference `p`, or nullptr if
+// it cannot (pageable host memory without pageable-memory access).
+const void* device_view(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  switch (a.type) {
+    case cudaMemoryTypeDevice:
+    case cudaMemoryTypeManaged:
+      return p;
+    case cudaMemoryTypeHost:
+      return a.devicePointer;
+    default: {
+      int dev = 0, pageable = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&pageable, cudaDevAttrPageableMemoryAccess, dev) != cudaSuccess)
+        return nullptr;
+      return pageable ? p : nullptr;
+    }
+  }
+}
+
+cf_status check_attention_params(const cf_paged_attention_params* p) {
+  if (p == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_seqs < 0 || p->num_heads <= 0 || p->num_kv_heads <= 0) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_heads % p->num_kv_heads != 0) return CF_ERR_INVALID_ARGUMENT;
+  if (dtype_bytes(p->dtype) == 0) return CF_ERR_INVALID_ARGUMENT;
+  if (p->max_context_len < 0 || p->max_blocks_per_seq < 0 || p->num_blocks < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (p->block_size <= 0 || p->head_dim <= 0) return CF_ERR_INVALID_ARGUMENT;
+  if (!cfb::attention_supported(p->head_dim, p->block_size, p->dtype)) return CF_ERR_UNSUPPORTED;
+  if (p->num_seqs == 0) return CF_OK;
+  if (p->num_seqs > 65535 || (int64_t)p->num_kv_heads * p->num_heads > 65535)
+    return CF_ERR_UNSUPPORTED;
+  if (p->max_blocks_per_seq < 1) return CF_ERR_INVALID_ARGUMENT;
+  if ((int64_t)p->max_context_len > (int64_t)p->max_blocks_per_seq * p->block_size)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (!p->query || !p->key_cache || !p->value_cache || !p->output || !p->block_tables ||
+      !p->context_lens)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->query) || !aligned16(p->key_cache) || !aligned16(p->value_cache) ||
+      !aligned16(p->output))
+    return CF_ERR_INVALID_ARGUMENT;
+  return CF_OK;
+}
+
+size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out) {
+  const int32_t split = v1_split_tokens();
+  if (split <= 0 || p->num_seqs <= 0 || p->max_context_len <= split) return 0;
+  const int64_t parts = (p->max_context_len + split - 1) / split;
+  if (parts_out) *parts_out = (int32_t)parts;
+  const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
+  // max + sum + output, each region rounded to 256 bytes.
+  auto round = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return (size_t)(2 * round(rows * 4) + round(rows * p->head_dim * 4));
+}
+
+}  // namespace
+}  // namespace cfb
+
+using namespace cfb;
+
+extern "C" {
+
+int32_t cf_abi_version(void) { return CF_ABI_VERSION; }
+
+int32_t cf_last_cuda_error(void) { return t_last_cuda_error; }
+
+const char* cf_status_string(cf_status status) {
+  switch (status) {
+    case CF_OK: return "ok";
+    case CF_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case CF_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case CF_ERR_WORKSPACE: return "workspace too small";
+    case CF_ERR_CUDA: return "CUDA runtime error";
+    case CF_ERR_PLAN: return "block-move plan would race";
+  }
+  return "unknown status";
+}
+
+size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) {
+  if (check_attention_params(p) != CF_OK) return 0;
+  return v1_split_bytes(p, nullptr);
+}
+
+cf_status cf_paged_attention_v1(const cf_paged_attention_params* p, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  cf_status st = check_attention_params(p);
+  if (st != CF_OK || p->num_seqs == 0) return st;
+  AttnLaunch l{p, 0, 1, nullptr, nullptr, nullptr, (cudaStream_t)stream};
+  int32_t parts = 0;
+  const size_t need = v1_split_bytes(p, &parts);
+  if (need > 0 && workspace != nullptr && workspace_bytes >= need) {
+    if (!aligned16(workspace)) return CF_ERR_INVALID_ARGUMENT;
+    const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
+    const int64_t r4 = (rows * 4 + 255) / 256 * 256;
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    l.part_tokens = v1_split_tokens();
+    l.num_parts = parts;
+    l.part_max = reinterpret_cast<float*>(w);
+    l.part_sum = reinterpret_cast<float*>(w + r4);
+    l.part_out = reinterpret_cast<float*>(w + 2 * r4);
+  }
+  return launch_paged_attention(l);
+}
+
+cf_status cf_paged_attention_v2(const cf_paged_attention_params* p, float* exp_sums,
+                                float* max_logits, float* tmp_output, int32_t num_partitions,
+                                void* stream) {
+  cf_status st = check_attention_params(p);
+  if (st != CF_OK || p->num_seqs == 0) return st;
+  if (!exp_sums || !max_logits || !tmp_output || num_partitions < 1)
+    return CF_ERR_INVALID_ARGUMENT;
+  const int64_t need = ((int64_t)p->max_context_len + kV2PartitionTokens - 1) / kV2PartitionTokens;
+  if (need > num_partitions) return CF_ERR_WORKSPACE;
+  AttnLaunch l{p, kV2PartitionTokens, num_partitions, max_logits, exp_sums, tmp_output,
+               (cudaStream_t)stream};
+  return launch_paged_attention(l);
+}
+
+cf_status cf_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                               void* value_cache, const int32_t* slot_mapping, int32_t num_tokens,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, int32_t dtype, void* stream) {
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0 || num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return CF_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping) return CF_ERR_INVALID_ARGUMENT;
+  const int64_t nb = num_blocks > 0 ? num_blocks : INT64_MAX / ((int64_t)block_size * 2);
+  return launch_reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, num_tokens,
+                                  num_kv_heads, (int64_t)head_dim * eb, block_size, nb,
+                                  (cudaStream_t)stream);
+}
+
+cf_status cf_copy_blocks(void* key_cache, void* value_cache, const int64_t* block_mapping,
+                         int32_t num_pairs, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t block_size, int64_t num_blocks, int32_t dtype, void* stream) {
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0 || num_pairs < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (num_pairs == 0) return CF_OK;
+  if (!key_cache || !value_cache || !block_mapping) return CF_ERR_INVALID_ARGUMENT;
+  const int64_t bb = (int64_t)num_kv_heads * block_size * head_dim * eb;
+  const int64_t nb = num_blocks > 0 ? num_blocks : INT64_MAX / bb;
+  return launch_copy_pairs64(key_cache, value_cache, block_mapping, num_pairs, bb, nb,
+                             (cudaStream_t)stream);
+}
+
+cf_status cf_swap_blocks(const void* src_cache, void* dst_cache, const int64_t* block_mapping,
+                         int32_t num_pairs, int64_t block_size_bytes, void* stream) {
+  if (num_pairs < 0 || block_size_bytes <= 0) return CF_ERR_INVALID_ARGUMENT;
+  if (num_pairs == 0) return CF_OK;
+  if (!src_cache || !dst_cache || !block_mapping) return CF_ERR_INVALID_ARGUMENT;
+  // The kernel dereferences all three pointers on the device: pageable host
+  // memory (CacheFlow's CPU pool is aligned_alloc, memory_pool.cpp:36) is
+  // refused here instead of faulting the GPU.
+  const void* dsrc = device_view(src_cache);
+  void* ddst = const_cast<void*>(device_view(dst_cache));
+  const int64_t* dmap = static_cast<const int64_t*>(device_view(block_mapping));
+  if (!dsrc || !ddst || !dmap) return CF_ERR_INVALID_ARGUMENT;
+  return launch_swap_pairs64(dsrc, ddst, dmap, num_pairs, block_size_bytes, (cudaStream_t)stream);
+}
+
+cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
+                             const int64_t* host_block_mapping, int32_t num_pairs,
+                             int64_t block_size_bytes, void* stream) {
+  if (num_pairs < 0 || block_size_bytes <= 0) return CF_ERR_INVALID_ARGUMENT;
+  if (num_pairs == 0) return CF_OK;
+  if (!src_cache || !dst_cache || !host_block_mapping) return CF_ERR_INVALID_ARGUMENT;
+  for (int32_t i = 0; i < num_pairs; ++i)
+    if (host_block_mapping[2 * i] < 0 || host_block_mapping[2 * i + 1] < 0)
+      return CF_ERR_INVALID_ARGUMENT;
+  const uint8_t* src = static_cast<const uint8_t*>(src_cache);
+  uint8_t* dst = static_cast<uint8_t*>(dst_cache);
+  int32_t i = 0;
+  while (i < num_pairs) {
+    const int64_t s0 = host_block_mapping[2 * i], d0 = host_block_mapping[2 * i + 1];
+    int32_t run = 1;
+    while (i + run < num_pairs && host_block_mapping[2 * (i + run)] == s0 + run &&
+           host_block_mapping[2 * (i + run) + 1] == d0 + run)
+      ++run;
+    cudaError_t e = cudaMemcpyAsync(dst + d0 * block_size_bytes, src + s0 * block_size_bytes,
+                                    (size_t)run * block_size_bytes, cudaMemcpyDefault,
+                                    (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    i += run;
+  }
+  return CF_OK;
+}
+
+cf_status cf_compact_kv_cache(void* key_cache, void* value_cache, const int32_t* src_block_ids,
+                              const int32_t* dst_block_ids, int32_t num_moves,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int64_t num_blocks, int32_t dtype, void* stream) {
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0 || num_moves < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (num_moves == 0) return CF_OK;
+  if (!key_cache || !value_cache || !src_block_ids || !dst_block_ids)
+    return CF_ERR_INVALID_ARGUMENT;
+  const int64_t bb = (int64_t)num_kv_heads * block_size * head_dim * eb;
+  const int64_t nb = num_blocks > 0 ? num_blocks : INT64_MAX / bb;
+  return launch_move_blocks32(key_cache, value_cache, src_block_ids, dst_block_ids, num_moves,
+                              bb, nb, (cudaStream_t)stream);
+}
+
+cf_status cf_memset_blocks(void* cache, const int32_t* block_ids, int32_t num_listed,
+                           int64_t block_size_bytes, int64_t num_blocks, void* stream) {
+  if (num_listed < 0 || block_size_bytes <= 0 || num_blocks < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (num_listed == 0) return CF_OK;
+  if (!cache || !block_ids) return CF_ERR_INVALID_ARGUMENT;
+  const int64_t nb = num_blocks > 0 ? num_blocks : INT64_MAX / block_size_bytes;
+  return launch_memset_blocks(cache, block_ids, num_listed, block_size_bytes, nb,
+                              (cudaStream_t)stream);
+}
+
+cf_status cf_compaction_plan(const uint8_t* used, int64_t num_blocks, int32_t* src_out,
+                             int32_t* dst_out, int32_t* num_moves) {
+  if (!used || !src_out || !dst_out || !num_moves || num_blocks < 0 || num_blocks > INT32_MAX)
+    return CF_ERR_INVALID_ARGUMENT;
+  int64_t live = 0;
+  for (int64_t b = 0; b < num_blocks; ++b) live += used[b] ? 1 : 0;
+  // Holes below `live` receive the live blocks found at or above `live`,
+  // both walked in increasing id order.
+  int64_t hole = 0, n = 0;
+  for (int64_t b = live; b < num_blocks; ++b) {
+    if (!used[b]) continue;
+    while (hole < live && used[hole]) ++hole;
+    src_out[n] = (int32_t)b;
+    dst_out[n] = (int32_t)hole;
+    ++n;
+    ++hole;
+  }
+  *num_moves = (int32_t)n;
+  return CF_OK;
+}
+
+cf_status cf_check_compaction_plan(const int32_t* src_ids, const int32_t* dst_ids,
+                                   int32_t num_moves, int64_t num_blocks) {
+  if (num_moves < 0 || num_blocks < 0 || num_blocks > INT32_MAX) return CF_ERR_INVALID_ARGUMENT;
+  if (num_moves == 0) return CF_OK;
+  if (!src_ids || !dst_ids) return CF_ERR_INVALID_ARGUMENT;
+  std::vector<uint8_t> role((size_t)num_blocks, 0);  // bit0: source, bit1: destination
+  for (int32_t i = 0; i < num_moves; ++i) {
+    const int32_t s = src_ids[i], d = dst_ids[i];
+    if (s < 0 || s >= num_blocks || d < 0 || d >= num_blocks) return CF_ERR_INVALID_ARGUMENT;
+    if (s == d) continue;  // skipped by the kernel
+    if (role[(size_t)d] & 2) return CF_ERR_PLAN;
+    role[(size_t)d] |= 2;
+    role[(size_t)s] |= 1;
+  }
+  for (int64_t b = 0; b < num_blocks; ++b)
+    if (role[(size_t)b] == 3) return CF_ERR_PLAN;
+  return CF_OK;
+}
+
+cf_status cf_get_device_errors(int32_t device, uint32_t* flags, int32_t clear) {
+  if (!flags) return CF_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  cf_status st = cuda_status(cudaGetDevice(&prev));
+  if (st != CF_OK) return st;
+  if ((st = cuda_status(cudaSetDevice(device))) != CF_OK) return st;
+  uint32_t bits = 0;
+  st = cuda_status(cudaDeviceSynchronize());
+  if (st == CF_OK) st = attention_read_errors(&bits, clear != 0);
+  if (st == CF_OK) st = cache_ops_read_errors(&bits, clear != 0);
+  cudaSetDevice(prev);
+  *flags = bits;
+  return st;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// CacheFlow's C++ entry points (fp32), same signatures as the reference.
+// ---------------------------------------------------------------------------
+namespace cacheflow {
+namespace cuda {
+
+namespace {
+thread_local int t_last_status = CF_OK;
+
+void note(cf_status st, const char* what) {
+  t_last_status = st;
+  if (st != CF_OK) {
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      std::fprintf(stderr, "cacheflow_b200: %s failed: %s\n", what, cf_status_string(st));
+    });
+  }
+}
+
+cf_paged_attention_params to_c(const PagedAttentionParams& p) {
+  cf_paged_attention_params c;
+  c.query = p.query;
+  c.key_cache = p.key_cache;
+  c.value_cache = p.value_cache;
+  c.output = p.output;
+  c.block_tables = p.block_tables;
+  c.context_lens = p.context_lens;
+  c.scale = p.scale;
+  c.num_seqs = p.num_seqs;
+  c.num_heads = p.num_heads;
+  c.num_kv_heads = p.num_kv_heads;
+  c.head_dim = p.head_dim;
+  c.block_size = p.block_size;
+  c.max_context_len = p.max_context_len;
+  c.max_blocks_per_seq = p.max_blocks_per_seq;
+  c.num_blocks = 0;
+  c.dtype = CF_F32;
+  return c;
+}
+}  // namespace
+
+int last_status() { return t_last_status; }
+
+void launch_paged_attention_v1(const PagedAttentionParams& params, cudaStream_t stream) {
+  cf_paged_attention_params c = to_c(params);
+  note(cf_paged_attention_v1(&c, nullptr, 0, stream), "launch_paged_attention_v1");
+}
+
+void launch_paged_attention_v2(const PagedAttentionParams& params, float* exp_sums,
+                               float* max_logits, float* tmp_output, int32_t num_partitions,
+                               cudaStream_t stream) {
+  cf_paged_attention_params c = to_c(params);
+  note(cf_paged_attention_v2(&c, exp_sums, max_logits, tmp_output, num_partitions, stream),
+       "launch_paged_attention_v2");
+}
+
+void launch_reshape_and_cache(const float* key, const float* value, float* key_cache,
+                              float* value_cache, const int32_t* slot_mapping, int32_t num_tokens,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              cudaStream_t stream) {
+  note(cf_reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, num_tokens,
+                            num_kv_heads, head_dim, block_size, 0, CF_F32, stream),
+       "launch_reshape_and_cache");
+}
+
+void launch_copy_blocks(float* key_cache, float* value_cache, const int64_t* block_mapping,
+                        int32_t num_pairs, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t block_size, cudaStream_t stream) {
+  note(cf_copy_blocks(key_cache, value_cache, block_mapping, num_pairs, num_kv_heads, head_dim,
+                      block_size, 0, CF_F32, stream),
+       "launch_copy_blocks");
+}
+
+void launch_swap_blocks(float* src_cache, float* dst_cache, const int64_t* block_mapping,
+                        int32_t num_pairs, int32_t block_size_bytes, cudaStream_t stream) {
+  note(cf_swap_blocks(src_cache, dst_cache, block_mapping, num_pairs, block_size_bytes, stream),
+       "launch_swap_blocks");
+}
+
+void launch_compact_kv_cache(float* key_cache, float* value_cache, const int32_t* src_block_ids,
+                             const int32_t* dst_block_ids, int32_t num_blocks,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                             cudaStream_t stream) {
+  note(cf_compact_kv_cache(key_cache, value_cache, src_block_ids, dst_block_ids, num_blocks,
+                           num_kv_heads, head_dim, block_size, 0, CF_F32, stream),
+       "launch_compact_kv_cache");
+}
+
+size_t get_gpu_free_memory() {
+  size_t f = 0, t = 0;
+  cudaMemGetInfo(&f, &t);
+  return f;
+}
+
+size_t get_gpu_total_memory() {
+  size_t f = 0, t = 0;
+  cudaMemGetInfo(&f, &t);
+  return t;
+}
+
+float get_gpu_memory_utilization() {
+  size_t f = 0, t = 0;
+  if (cudaMemGetInfo(&f, &t) != cudaSuccess || t == 0) return 0.f;
+  return 1.0f - (float)f / (float)t;
+}
+
+void async_memcpy_h2d(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  note(cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream)),
+       "async_memcpy_h2d");
+}
+
+void async_memcpy_d2h(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  note(cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, stream)),
+       "async_memcpy_d2h");
+}
+
+void async_memcpy_d2d(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  note(cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream)),
+       "async_memcpy_d2d");
+}
+
+void launch_memset_blocks(float* cache, const int32_t* block_ids, int32_t num_blocks,
+                          int32_t block_size_bytes, cudaStream_t stream) {
+  note(cf_memset_blocks(cache, block_ids, num_blocks, block_size_bytes, 0, stream),
+       "launch_memset_blocks");
+}
+
+void synchronize_stream(cudaStream_t stream) { cudaStreamSynchronize(stream); }
+
+void synchronize_device() { cudaDeviceSynchronize(); }
+
+}  // namespace cuda
+}  // namespace cacheflow

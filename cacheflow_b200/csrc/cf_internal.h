@@ -1,0 +1,58 @@
+// cf_internal.h -- host-side declarations shared by the library's translation
+// units (launchers, per-TU device error words, status helpers).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cacheflow_b200.h"
+
+namespace cfb {
+
+// Records the CUDA error (thread-local) and maps it to a status.
+cf_status cuda_status(cudaError_t err);
+
+// Checks the launch that was just issued.
+inline cf_status check_launch() { return cuda_status(cudaGetLastError()); }
+
+inline int dtype_bytes(int32_t dtype) {
+  return dtype == CF_F32 ? 4 : (dtype == CF_F16 || dtype == CF_BF16) ? 2 : 0;
+}
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---- paged attention (paged_attention.cu) ---------------------------------
+struct AttnLaunch {
+  const cf_paged_attention_params* p;
+  int32_t part_tokens;  // tokens per partition; <= 0: one partition per sequence
+  int32_t num_parts;    // partition stride of the scratch arrays
+  float* part_max;      // [num_seqs, num_heads, num_parts] or null (unsplit)
+  float* part_sum;
+  float* part_out;      // [num_seqs, num_heads, num_parts, head_dim]
+  cudaStream_t stream;
+};
+cf_status launch_paged_attention(const AttnLaunch& l);
+bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype);
+cf_status attention_read_errors(uint32_t* bits, bool clear);
+
+// ---- KV-cache data movement (cache_ops.cu) ---------------------------------
+cf_status launch_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                                   void* value_cache, const int32_t* slot_mapping,
+                                   int32_t num_tokens, int32_t num_kv_heads, int64_t row_bytes,
+                                   int32_t block_size, int64_t num_blocks, cudaStream_t stream);
+cf_status launch_copy_pairs64(void* key_cache, void* value_cache, const int64_t* mapping,
+                              int32_t num_pairs, int64_t block_bytes, int64_t num_blocks,
+                              cudaStream_t stream);
+cf_status launch_swap_pairs64(const void* src_cache, void* dst_cache, const int64_t* mapping,
+                              int32_t num_pairs, int64_t block_bytes, cudaStream_t stream);
+cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t* src_ids,
+                               const int32_t* dst_ids, int32_t num_moves, int64_t block_bytes,
+                               int64_t num_blocks, cudaStream_t stream);
+cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_listed,
+                               int64_t block_bytes, int64_t num_blocks, cudaStream_t stream);
+cf_status cache_ops_read_errors(uint32_t* bits, bool clear);
+
+}  // namespace cfb

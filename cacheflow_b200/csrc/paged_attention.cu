@@ -1,0 +1,600 @@
+// paged_attention.cu -- ragged-batch paged decode attention for sm_100a.
+//
+// Semantics (one query token per sequence), following CacheFlow
+// src/cacheflow/cuda/paged_attention.cu:
+//   kv head of query head h      = h / (num_heads / num_kv_heads)      (:58)
+//   logical block b of sequence s = block_tables[s * max_blocks_per_seq + b] (:78-79)
+//   K row of token t              = key_cache[((phys * Hkv + kvh) * 16 + t % 16) * D]  (:85-87)
+//   V row                         = value_cache[same index]                          (:151-153)
+//   out[s, h, :] = softmax_t(scale * q . k_t) . V  over t < context_lens[s]
+// computed as the normalised softmax the reference intends (its V1 overflows
+// a 128-entry shared array past 128 tokens and its V2 leaves the result
+// unnormalised; neither is reproduced).
+//
+// Design:
+//   * One CTA per (partition, kv head [x head chunk], sequence).  All query
+//     heads of a GQA group are handled by the CTA that streams their KV head,
+//     so every KV byte is read from HBM once per KV head.
+//   * Each of the NW warps streams its own share of the partition's 16-token
+//     blocks through a private S-stage ring in shared memory.  Lane 0 of the
+//     warp issues 1-D bulk async copies (TMA, cp.async.bulk) of the 4 KB
+//     (bf16/fp16, D=128) K and V tiles of a block, completion tracked by one
+//     mbarrier per stage; the warp computes on stage i while stages i+1..i+S-1
+//     are in flight.  Block-table entries are fetched 32 at a time by the warp
+//     and broadcast with shuffles.
+//   * Per warp: online softmax in the log2 domain (q pre-scaled by
+//     scale*log2(e)), QK dot products by 8-lane groups with xor-shuffle
+//     reductions, PV with each lane owning D/32 output columns.
+//   * Warps are merged through shared memory at the end of the partition.
+//     A sequence that fits one partition writes its output directly;
+//     otherwise the partition writes (max logit, exp-sum, normalised partial
+//     output) and the reduce kernel merges partitions with the log-sum-exp
+//     weights  w_p = exp_sum_p * exp(max_p - max).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "cf_device.cuh"
+#include "cf_internal.h"
+
+namespace cfb {
+
+__device__ uint32_t g_attn_errors;
+
+__device__ __forceinline__ void attn_error(uint32_t bits) { atomicOr(&g_attn_errors, bits); }
+
+constexpr int kBlockTokens = 16;  // KV block size (tokens); CacheFlow's KV_BLOCK_SIZE
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct AttnArgs {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  void* out;
+  const int32_t* block_tables;
+  const int32_t* context_lens;
+  float* part_max;  // [S, H, P]  natural-log units; null when unsplit
+  float* part_sum;  // [S, H, P]
+  float* part_out;  // [S, H, P, D]
+  float scale_log2;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t group;        // num_heads / num_kv_heads
+  int32_t head_chunks;  // ceil(group / HG)
+  int32_t max_blocks_per_seq;
+  int32_t part_blocks;  // KV blocks per partition
+  int32_t num_parts;    // partition stride of the scratch
+  int64_t num_blocks;   // pool size (checked range of physical ids)
+};
+
+// ---------------------------------------------------------------------------
+// FMA consumer: QK by 8-lane groups (each lane reads D*sizeof(T)/128 16-byte
+// chunks of a K row: the 8 lanes of a group cover 128 contiguous bytes, so
+// shared-memory reads are conflict-free without swizzling), PV with lane l
+// owning columns [l*D/32, (l+1)*D/32).
+// ---------------------------------------------------------------------------
+template <typename T, int D, int HG>
+struct FmaConsumer {
+  static constexpr int kVec = 16 / (int)sizeof(T);           // elements per 16 B
+  static constexpr int kChunks = D * (int)sizeof(T) / 128;   // 16 B chunks per lane (QK)
+  static constexpr int kEpl = D / 32;                        // columns per lane (PV)
+  static_assert(kChunks >= 1, "head_dim too small for this element type");
+
+  float q[HG][kChunks * kVec];
+  float o[HG][kEpl];
+  float m[HG];
+  float l[HG];
+
+  __device__ __forceinline__ void init(const T* qrow, int nheads, float scale_log2, int lane) {
+    const int i = lane & 7;
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) {
+        if (h < nheads) {
+          load_widen<T, kVec>(qrow + (size_t)h * D + (i + 8 * k) * kVec, &q[h][k * kVec]);
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) q[h][k * kVec + e] *= scale_log2;
+        } else {
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) q[h][k * kVec + e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kEpl; ++e) o[h][e] = 0.f;
+      m[h] = -INFINITY;
+      l[h] = 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void pv_token(const T* vrow, const float* pt_h, int t) {
+    float vf[kEpl];
+    load_widen<T, kEpl>(vrow + t * D, vf);
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      const float pt = pt_h[h * kBlockTokens + t];
+#pragma unroll
+      for (int e = 0; e < kEpl; ++e) o[h][e] = fmaf(pt, vf[e], o[h][e]);
+    }
+  }
+
+  // One 16-token block; `ntok` valid tokens (1..16).  `pbuf` is this warp's
+  // HG*16-float scratch.
+  __device__ __forceinline__ void block(const T* kt, const T* vt, int ntok, float* pbuf,
+                                        int lane) {
+    const int j = lane >> 3;
+    const int i = lane & 7;
+    float s[4][HG];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int tok = p * 4 + j;
+      const T* row = kt + tok * D;
+      float acc[HG];
+#pragma unroll
+      for (int h = 0; h < HG; ++h) acc[h] = 0.f;
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) {
+        float kf[kVec];
+        load_widen<T, kVec>(row + (i + 8 * k) * kVec, kf);
+#pragma unroll
+        for (int h = 0; h < HG; ++h)
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) acc[h] = fmaf(q[h][k * kVec + e], kf[e], acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        float a = acc[h];
+        a += shfl_xor(a, 1);
+        a += shfl_xor(a, 2);
+        a += shfl_xor(a, 4);
+        s[p][h] = (tok < ntok) ? a : -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      float bm = fmaxf(fmaxf(s[0][h], s[1][h]), fmaxf(s[2][h], s[3][h]));
+      bm = fmaxf(bm, shfl_xor(bm, 8));
+      bm = fmaxf(bm, shfl_xor(bm, 16));
+      const float mn = fmaxf(m[h], bm);
+      const float mu = (mn == -INFINITY) ? 0.f : mn;
+      const float alpha = exp2f(m[h] - mu);
+      m[h] = mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        s[p][h] = exp2f(s[p][h] - mu);
+        ps += s[p][h];
+      }
+      ps += shfl_xor(ps, 8);
+      ps += shfl_xor(ps, 16);
+      l[h] = l[h] * alpha + ps;
+#pragma unroll
+      for (int e = 0; e < kEpl; ++e) o[h][e] *= alpha;
+      if (i == 0) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) pbuf[h * kBlockTokens + p * 4 + j] = s[p][h];
+      }
+    }
+    __syncwarp();
+    const T* vrow = vt + lane * kEpl;
+    if (ntok == kBlockTokens) {
+#pragma unroll
+      for (int t = 0; t < kBlockTokens; ++t) pv_token(vrow, pbuf, t);
+    } else {
+#pragma unroll 1
+      for (int t = 0; t < ntok; ++t) pv_token(vrow, pbuf, t);
+    }
+  }
+
+  // Per-warp result into the merge area: o[h][d] (unnormalised), m, l.
+  __device__ __forceinline__ void store(float* mo, float* mm, float* ml, int lane) {
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+#pragma unroll
+      for (int e = 0; e < kEpl; ++e) mo[h * D + lane * kEpl + e] = o[h][e];
+      if (lane == 0) {
+        mm[h] = m[h];
+        ml[h] = l[h];
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Kernel configuration (per element type / head dim).
+// ---------------------------------------------------------------------------
+template <typename T, int D, int HG>
+struct AttnConfig {
+  static constexpr int kTileBytes = kBlockTokens * D * (int)sizeof(T);  // one K or V tile
+  static constexpr int kWarps = 4;
+  static constexpr int kStageBudget = 96 * 1024;
+  static constexpr int kStagesRaw = kStageBudget / (kWarps * 2 * kTileBytes);
+  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
+  static constexpr int kTileArea = kWarps * kStages * 2 * kTileBytes;
+  static constexpr int kMergeBytes = kWarps * HG * (D + 2) * 4;
+  static_assert(kMergeBytes <= kTileArea, "merge area must fit in the stage area");
+  static constexpr int kBarOffset = kTileArea;
+  static constexpr int kFlagOffset = kBarOffset + kWarps * kStages * 8;
+  static constexpr int kPbufOffset = kFlagOffset + ((kWarps * kStages * 4 + 15) / 16) * 16;
+  static constexpr int kSmemBytes = kPbufOffset + kWarps * HG * kBlockTokens * 4;
+  static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
+};
+
+template <typename T, int D, int HG>
+__global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
+    paged_attention_kernel(const AttnArgs a) {
+  using Cfg = AttnConfig<T, D, HG>;
+  constexpr int NW = Cfg::kWarps;
+  constexpr int S = Cfg::kStages;
+  constexpr int TILE = Cfg::kTileBytes;
+
+  const int part = blockIdx.x;
+  const int kvh = blockIdx.y / a.head_chunks;
+  const int chunk = blockIdx.y - kvh * a.head_chunks;
+  const int seq = blockIdx.z;
+  const int head0 = kvh * a.group + chunk * HG;
+  const int nheads = min(HG, a.group - chunk * HG);
+
+  int ctx = a.context_lens[seq];
+  const int ctx_cap = a.max_blocks_per_seq * kBlockTokens;
+  if (ctx < 0 || ctx > ctx_cap) {
+    if (threadIdx.x == 0 && part == 0 && blockIdx.y == 0) attn_error(CF_DEVERR_CONTEXT_LEN);
+    ctx = ctx < 0 ? 0 : ctx_cap;
+  }
+  const int nblk = (ctx + kBlockTokens - 1) / kBlockTokens;
+  const int nparts = nblk == 0 ? 1 : (nblk + a.part_blocks - 1) / a.part_blocks;
+  if (part >= nparts) return;  // whole CTA: this sequence is shorter
+  if (part == 0 && nparts > (int)gridDim.x && threadIdx.x == 0 && blockIdx.y == 0)
+    attn_error(CF_DEVERR_CONTEXT_LEN);  // context_lens exceeds max_context_len
+  const bool single = (nparts == 1);
+  const int pb0 = part * a.part_blocks;
+  const int pb1 = min(nblk, pb0 + a.part_blocks);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint8_t* tiles = smem + (size_t)warp * S * 2 * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset) + warp * S;
+  int* flags = reinterpret_cast<int*>(smem + Cfg::kFlagOffset) + warp * S;
+  float* pbuf = reinterpret_cast<float*>(smem + Cfg::kPbufOffset) + warp * HG * kBlockTokens;
+
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  FmaConsumer<T, D, HG> cons;
+  const T* qrow = reinterpret_cast<const T*>(a.q) + ((size_t)seq * a.num_heads + head0) * D;
+  cons.init(qrow, nheads, a.scale_log2, lane);
+
+  // This warp's blocks: pb0 + warp + j*NW, j in [0, nb).
+  const int span = pb1 - pb0;
+  const int nb = span > warp ? (span - warp + NW - 1) / NW : 0;
+  const int32_t* table = a.block_tables + (size_t)seq * a.max_blocks_per_seq + pb0 + warp;
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k_cache);
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v_cache);
+
+  auto fetch_ids = [&](int jbase) -> int {
+    const int j = jbase + lane;
+    return j < nb ? table[(size_t)j * NW] : 0;
+  };
+  auto issue = [&](int j, int phys) {  // lane 0 only
+    const int s = j % S;
+    const uint32_t bar = smem_addr(&bars[s]);
+    if (phys < 0 || (int64_t)phys >= a.num_blocks) {
+      attn_error(CF_DEVERR_BLOCK_ID);
+      flags[s] = 0;
+      mbar_arrive(bar);
+      return;
+    }
+    flags[s] = 1;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, 2 * TILE);
+    const size_t off = ((size_t)phys * a.num_kv_heads + kvh) * (size_t)TILE;
+    uint8_t* kt = tiles + (size_t)s * 2 * TILE;
+    bulk_load(smem_addr(kt), kbase + off, TILE, bar);
+    bulk_load(smem_addr(kt + TILE), vbase + off, TILE, bar);
+  };
+
+  int ids = fetch_ids(0);
+  const int pro = nb < S ? nb : S;
+  for (int j = 0; j < pro; ++j) {
+    const int phys = __shfl_sync(0xffffffffu, ids, j);
+    if (lane == 0) issue(j, phys);
+  }
+
+  bool ok = true;
+  for (int i = 0; i < nb; ++i) {
+    const int s = i % S;
+    const uint32_t parity = (uint32_t)(i / S) & 1u;
+    const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), parity);
+    if (!__all_sync(0xffffffffu, ready)) {
+      // A copy never completed: record it, wait (bounded) for every copy this
+      // warp still has in flight so none lands after the CTA exits, and stop.
+      if (lane == 0) {
+        attn_error(CF_DEVERR_TIMEOUT);
+        const int last = (i + S < nb ? i + S : nb);
+        for (int k = i; k < last; ++k)
+          mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u);
+      }
+      __syncwarp();
+      ok = false;
+      break;
+    }
+    const int blk = pb0 + warp + i * NW;
+    const int ntok = min(kBlockTokens, ctx - blk * kBlockTokens);
+    if (flags[s]) {
+      const T* kt = reinterpret_cast<const T*>(tiles + (size_t)s * 2 * TILE);
+      cons.block(kt, kt + TILE / (int)sizeof(T), ntok, pbuf, lane);
+    }
+    __syncwarp();
+    const int jn = i + S;
+    if (jn < nb) {
+      if ((jn & 31) == 0) ids = fetch_ids(jn);
+      const int phys = __shfl_sync(0xffffffffu, ids, jn & 31);
+      if (lane == 0) issue(jn, phys);
+    }
+  }
+
+  grid_dependency_launch();
+
+  // Merge the warps' partial softmax states.
+  __syncthreads();  // every warp is done with its stage tiles
+  float* mo = reinterpret_cast<float*>(smem);
+  float* mm = mo + NW * HG * D;
+  float* ml = mm + NW * HG;
+  cons.store(mo + warp * HG * D, mm + warp * HG, ml + warp * HG, lane);
+  const int all_ok = __syncthreads_and(ok ? 1 : 0);
+  if (!all_ok) return;
+
+  const size_t H = (size_t)a.num_heads;
+  for (int idx = threadIdx.x; idx < nheads * D; idx += NW * 32) {
+    const int h = idx / D;
+    const int d = idx - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, mm[w * HG + h]);
+    float L = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float sc = exp2f(mm[w * HG + h] - M);
+        L = fmaf(ml[w * HG + h], sc, L);
+        acc = fmaf(mo[(w * HG + h) * D + d], sc, acc);
+      }
+    }
+    const float res = L > 0.f ? acc / L : 0.f;
+    const size_t hq = (size_t)seq * H + head0 + h;
+    if (single) {
+      reinterpret_cast<T*>(a.out)[hq * D + d] = from_float<T>(res);
+    } else {
+      const size_t pi = hq * a.num_parts + part;
+      a.part_out[pi * D + d] = res;
+      if (d == 0) {
+        a.part_max[pi] = M * kLn2;
+        a.part_sum[pi] = L;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Partition reduce: one CTA of D threads per (query head, sequence).
+// out = sum_p w_p * o_p / sum_p w_p,  w_p = exp_sum_p * exp(max_p - max).
+// Sequences with a single partition were written by the partition kernel.
+// ---------------------------------------------------------------------------
+struct ReduceArgs {
+  void* out;
+  const float* part_max;
+  const float* part_sum;
+  const float* part_out;
+  const int32_t* context_lens;
+  int32_t num_heads;
+  int32_t max_blocks_per_seq;
+  int32_t part_blocks;
+  int32_t num_parts;      // scratch stride
+  int32_t launched_parts; // partitions the partition kernel covered
+};
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < nw; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  __syncthreads();
+  return r;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(D) paged_attention_reduce_kernel(const ReduceArgs r) {
+  grid_dependency_wait();
+  const int h = blockIdx.x;
+  const int seq = blockIdx.y;
+  int ctx = r.context_lens[seq];
+  const int cap = r.max_blocks_per_seq * kBlockTokens;
+  ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
+  const int nblk = (ctx + kBlockTokens - 1) / kBlockTokens;
+  int nparts = nblk == 0 ? 1 : (nblk + r.part_blocks - 1) / r.part_blocks;
+  if (nparts <= 1) return;
+  if (nparts > r.launched_parts) nparts = r.launched_parts;
+
+  extern __shared__ float wsh[];  // nparts weights
+  __shared__ float red[32];
+  const size_t base = ((size_t)seq * r.num_heads + h) * r.num_parts;
+  float lm = -INFINITY;
+  for (int p = threadIdx.x; p < nparts; p += blockDim.x) lm = fmaxf(lm, r.part_max[base + p]);
+  const float M = block_reduce(lm, true, red);
+  float ls = 0.f;
+  for (int p = threadIdx.x; p < nparts; p += blockDim.x) {
+    const float w = (M == -INFINITY) ? 0.f : r.part_sum[base + p] * expf(r.part_max[base + p] - M);
+    wsh[p] = w;
+    ls += w;
+  }
+  const float L = block_reduce(ls, false, red);  // also orders the wsh writes
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    const float* po = r.part_out + base * D + d;
+    for (int p = 0; p < nparts; ++p) acc = fmaf(wsh[p], po[(size_t)p * D], acc);
+    reinterpret_cast<T*>(r.out)[((size_t)seq * r.num_heads + h) * D + d] =
+        from_float<T>(L > 0.f ? acc / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+namespace {
+
+template <typename K>
+cf_status ensure_smem(K kern, int bytes) {
+  // Per-device opt-in to more than 48 KB of dynamic shared memory.
+  static std::once_flag flags[64];
+  static cudaError_t errs[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64)
+    return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  std::call_once(flags[dev], [&] {
+    errs[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  return cuda_status(errs[dev]);
+}
+
+template <typename T, int D, int HG>
+cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x) {
+  using Cfg = AttnConfig<T, D, HG>;
+  const cf_paged_attention_params& p = *l.p;
+  a.head_chunks = (a.group + HG - 1) / HG;
+  auto kern = paged_attention_kernel<T, D, HG>;
+  cf_status st = ensure_smem(kern, Cfg::kSmemAlloc);
+  if (st != CF_OK) return st;
+  dim3 grid((unsigned)grid_x, (unsigned)(p.num_kv_heads * a.head_chunks), (unsigned)p.num_seqs);
+  kern<<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a);
+  st = check_launch();
+  if (st != CF_OK || l.part_max == nullptr || grid_x == 1) return st;
+
+  ReduceArgs r;
+  r.out = p.output;
+  r.part_max = l.part_max;
+  r.part_sum = l.part_sum;
+  r.part_out = l.part_out;
+  r.context_lens = p.context_lens;
+  r.num_heads = p.num_heads;
+  r.max_blocks_per_seq = p.max_blocks_per_seq;
+  r.part_blocks = a.part_blocks;
+  r.num_parts = l.num_parts;
+  r.launched_parts = grid_x;
+  const size_t rsmem = (size_t)grid_x * sizeof(float);
+  if (rsmem > 48 * 1024) return CF_ERR_UNSUPPORTED;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
+  cfg.blockDim = dim3(D);
+  cfg.dynamicSmemBytes = rsmem;
+  cfg.stream = l.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_reduce_kernel<T, D>, r));
+}
+
+template <typename T, int D>
+cf_status launch_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
+  if (a.group == 1) return launch_typed<T, D, 1>(l, a, grid_x);
+  if (a.group == 2) return launch_typed<T, D, 2>(l, a, grid_x);
+  return launch_typed<T, D, 4>(l, a, grid_x);
+}
+
+template <typename T>
+cf_status launch_type(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
+  switch (l.p->head_dim) {
+    case 64: return launch_dim<T, 64>(l, a, grid_x);
+    case 128: return launch_dim<T, 128>(l, a, grid_x);
+    case 256:
+      if constexpr (sizeof(T) == 2) return launch_dim<T, 256>(l, a, grid_x);
+      return CF_ERR_UNSUPPORTED;
+    default: return CF_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype) {
+  if (block_size != kBlockTokens) return false;
+  if (dtype == CF_F32) return head_dim == 64 || head_dim == 128;
+  if (dtype == CF_F16 || dtype == CF_BF16)
+    return head_dim == 64 || head_dim == 128 || head_dim == 256;
+  return false;
+}
+
+cf_status launch_paged_attention(const AttnLaunch& l) {
+  const cf_paged_attention_params& p = *l.p;
+  if (p.num_seqs == 0) return CF_OK;
+  AttnArgs a;
+  a.q = p.query;
+  a.k_cache = p.key_cache;
+  a.v_cache = p.value_cache;
+  a.out = p.output;
+  a.block_tables = p.block_tables;
+  a.context_lens = p.context_lens;
+  a.part_max = l.part_max;
+  a.part_sum = l.part_sum;
+  a.part_out = l.part_out;
+  a.scale_log2 = p.scale * kLog2e;
+  a.num_heads = p.num_heads;
+  a.num_kv_heads = p.num_kv_heads;
+  a.group = p.num_heads / p.num_kv_heads;
+  a.head_chunks = 1;
+  a.max_blocks_per_seq = p.max_blocks_per_seq;
+  a.num_blocks = p.num_blocks > 0 ? p.num_blocks : INT64_MAX;
+  int grid_x = 1;
+  if (l.part_tokens > 0 && l.part_max != nullptr) {
+    a.part_blocks = l.part_tokens / kBlockTokens;
+    a.num_parts = l.num_parts;
+    const int need = (p.max_context_len + l.part_tokens - 1) / l.part_tokens;
+    grid_x = need < 1 ? 1 : need;
+    if (grid_x > l.num_parts) return CF_ERR_WORKSPACE;
+  } else {
+    a.part_blocks = p.max_blocks_per_seq > 0 ? p.max_blocks_per_seq : 1;
+    a.num_parts = 1;
+    a.part_max = a.part_sum = a.part_out = nullptr;
+  }
+  AttnLaunch l2 = l;
+  if (a.part_max == nullptr) l2.part_max = nullptr;
+  switch (p.dtype) {
+    case CF_F32: return launch_type<float>(l2, a, grid_x);
+    case CF_F16: return launch_type<__half>(l2, a, grid_x);
+    case CF_BF16: return launch_type<__nv_bfloat16>(l2, a, grid_x);
+    default: return CF_ERR_UNSUPPORTED;
+  }
+}
+
+cf_status attention_read_errors(uint32_t* bits, bool clear) {
+  uint32_t v = 0;
+  cf_status s = cuda_status(cudaMemcpyFromSymbol(&v, g_attn_errors, sizeof(v)));
+  if (s != CF_OK) return s;
+  *bits |= v;
+  if (clear) {
+    const uint32_t zero = 0;
+    s = cuda_status(cudaMemcpyToSymbol(g_attn_errors, &zero, sizeof(zero)));
+  }
+  return s;
+}
+
+}  // namespace cfb

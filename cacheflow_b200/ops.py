@@ -1,0 +1,264 @@
+"""PyTorch-facing operators over the C ABI.
+
+One function per CacheFlow operator (src/cacheflow/cuda/*.cuh), same names and
+argument meaning; tensors are CUDA tensors in CacheFlow's layouts:
+
+    query / output   [num_seqs, num_heads, head_dim]
+    key/value_cache  [num_blocks, num_kv_heads, block_size, head_dim]
+    block_tables     int32 [num_seqs, max_blocks_per_seq]
+    context_lens     int32 [num_seqs]
+
+Every call is asynchronous on the current CUDA stream.  A non-OK status of the
+library raises CacheFlowError; there is no fallback path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import AttentionParams, CacheFlowError, check
+
+__all__ = [
+    "CacheFlowError",
+    "paged_attention_v1",
+    "paged_attention_v1_workspace_size",
+    "paged_attention_v2",
+    "v2_num_partitions",
+    "reshape_and_cache",
+    "copy_blocks",
+    "swap_blocks",
+    "swap_blocks_dma",
+    "compact_kv_cache",
+    "memset_blocks",
+    "compaction_plan",
+    "check_compaction_plan",
+    "device_errors",
+    "dtype_code",
+]
+
+V2_PARTITION_TOKENS = 512
+
+_DTYPES = {torch.float32: _lib.CF_F32, torch.float16: _lib.CF_F16, torch.bfloat16: _lib.CF_BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise CacheFlowError(_lib.CF_ERR_UNSUPPORTED, f"dtype {dt}") from None
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                      max_context_len) -> AttentionParams:
+    for name, t in (("out", out), ("query", query), ("key_cache", key_cache),
+                    ("value_cache", value_cache), ("block_tables", block_tables),
+                    ("context_lens", context_lens)):
+        if not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, f"{name} must be contiguous")
+    if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "block_tables/context_lens must be int32")
+    if not (query.dtype == key_cache.dtype == value_cache.dtype == out.dtype):
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "query, caches and output must share a dtype")
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    p = AttentionParams()
+    p.query = _ptr(query)
+    p.key_cache = _ptr(key_cache)
+    p.value_cache = _ptr(value_cache)
+    p.output = _ptr(out)
+    p.block_tables = _ptr(block_tables)
+    p.context_lens = _ptr(context_lens)
+    p.scale = float(scale)
+    p.num_seqs = query.shape[0]
+    p.num_heads = query.shape[1]
+    p.num_kv_heads = num_kv_heads
+    p.head_dim = head_dim
+    p.block_size = block_size
+    p.max_context_len = int(max_context_len)
+    p.max_blocks_per_seq = block_tables.shape[1] if block_tables.dim() == 2 else 0
+    p.num_blocks = num_blocks
+    p.dtype = dtype_code(query.dtype)
+    return p
+
+
+def paged_attention_v1_workspace_size(query, key_cache, block_tables, max_context_len) -> int:
+    """Bytes of optional workspace that lets paged_attention_v1 split long contexts."""
+    lib = _lib.load()
+    p = AttentionParams()
+    p.num_seqs = query.shape[0]
+    p.num_heads = query.shape[1]
+    _, p.num_kv_heads, p.block_size, p.head_dim = key_cache.shape
+    p.max_context_len = int(max_context_len)
+    p.max_blocks_per_seq = block_tables.shape[1]
+    p.num_blocks = key_cache.shape[0]
+    p.dtype = dtype_code(query.dtype)
+    return int(lib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)))
+
+
+def paged_attention_v1(out, query, key_cache, value_cache, block_tables, context_lens, scale=None,
+                       max_context_len=None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention (launch_paged_attention_v1, paged_attention.cuh:44-46)."""
+    lib = _lib.load()
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len)
+    ws = _ptr(workspace)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib.cf_paged_attention_v1(ctypes.byref(p), ws, ws_bytes, _stream(query)),
+          "cf_paged_attention_v1")
+    return out
+
+
+def v2_num_partitions(max_context_len: int) -> int:
+    return max(1, (int(max_context_len) + V2_PARTITION_TOKENS - 1) // V2_PARTITION_TOKENS)
+
+
+def paged_attention_v2(out, exp_sums, max_logits, tmp_output, query, key_cache, value_cache,
+                       block_tables, context_lens, scale=None, max_context_len=None) -> torch.Tensor:
+    """Partitioned decode attention + reduce (launch_paged_attention_v2, paged_attention.cuh:48-54).
+
+    exp_sums / max_logits: float32 [num_seqs, num_heads, P];
+    tmp_output: float32 [num_seqs, num_heads, P, head_dim]; P >= v2_num_partitions(max_context_len).
+    """
+    lib = _lib.load()
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len)
+    for t in (exp_sums, max_logits, tmp_output):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "v2 scratch must be contiguous float32")
+    parts = exp_sums.shape[-1]
+    check(lib.cf_paged_attention_v2(ctypes.byref(p), _ptr(exp_sums), _ptr(max_logits),
+                                    _ptr(tmp_output), parts, _stream(query)),
+          "cf_paged_attention_v2")
+    return out
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping) -> None:
+    """Scatter new K/V rows into their slots (launch_reshape_and_cache, kv_cache_kernels.cuh:17-27)."""
+    lib = _lib.load()
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    if slot_mapping.dtype != torch.int32:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "slot_mapping must be int32")
+    check(lib.cf_reshape_and_cache(_ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache),
+                                   _ptr(slot_mapping), key.shape[0], num_kv_heads, head_dim,
+                                   block_size, num_blocks, dtype_code(key_cache.dtype),
+                                   _stream(key_cache)),
+          "cf_reshape_and_cache")
+
+
+def copy_blocks(key_cache, value_cache, block_mapping) -> None:
+    """COW block copies (launch_copy_blocks, kv_cache_kernels.cuh:29-37); block_mapping int64 [N, 2]."""
+    lib = _lib.load()
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    if block_mapping.dtype != torch.int64:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "block_mapping must be int64")
+    check(lib.cf_copy_blocks(_ptr(key_cache), _ptr(value_cache), _ptr(block_mapping),
+                             block_mapping.shape[0], num_kv_heads, head_dim, block_size,
+                             num_blocks, dtype_code(key_cache.dtype), _stream(key_cache)),
+          "cf_copy_blocks")
+
+
+def _block_bytes(cache: torch.Tensor) -> int:
+    return cache[0].numel() * cache.element_size()
+
+
+def swap_blocks(src, dst, block_mapping, stream_tensor: torch.Tensor | None = None) -> None:
+    """SM-driven block copy between caches (launch_swap_blocks, kv_cache_kernels.cuh:39-45).
+
+    One of src/dst may be pinned host memory; block_mapping int64 [N, 2] must be
+    device-readable (a CUDA tensor or pinned host tensor).
+    """
+    lib = _lib.load()
+    dev_t = stream_tensor if stream_tensor is not None else (src if src.is_cuda else dst)
+    check(lib.cf_swap_blocks(_ptr(src), _ptr(dst), _ptr(block_mapping), block_mapping.shape[0],
+                             _block_bytes(src), _stream(dev_t)),
+          "cf_swap_blocks")
+
+
+def swap_blocks_dma(src, dst, block_mapping_host: np.ndarray | torch.Tensor,
+                    stream_tensor: torch.Tensor | None = None) -> None:
+    """Copy-engine swap: block_mapping in host memory, consecutive runs merged."""
+    lib = _lib.load()
+    m = block_mapping_host
+    if isinstance(m, torch.Tensor):
+        m = m.cpu().numpy()
+    m = np.ascontiguousarray(m, dtype=np.int64)
+    dev_t = stream_tensor if stream_tensor is not None else (src if src.is_cuda else dst)
+    check(lib.cf_swap_blocks_dma(_ptr(src), _ptr(dst), m.ctypes.data, m.shape[0], _block_bytes(src),
+                                 _stream(dev_t)),
+          "cf_swap_blocks_dma")
+
+
+def compact_kv_cache(key_cache, value_cache, src_block_ids, dst_block_ids) -> None:
+    """In-place defragmentation moves (launch_compact_kv_cache, kv_cache_kernels.cuh:47-56)."""
+    lib = _lib.load()
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    if src_block_ids.dtype != torch.int32 or dst_block_ids.dtype != torch.int32:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "block ids must be int32")
+    check(lib.cf_compact_kv_cache(_ptr(key_cache), _ptr(value_cache), _ptr(src_block_ids),
+                                  _ptr(dst_block_ids), src_block_ids.shape[0], num_kv_heads,
+                                  head_dim, block_size, num_blocks, dtype_code(key_cache.dtype),
+                                  _stream(key_cache)),
+          "cf_compact_kv_cache")
+
+
+def memset_blocks(cache, block_ids) -> None:
+    """Zero listed blocks (launch_memset_blocks, memory_utils.cuh:28-33)."""
+    lib = _lib.load()
+    check(lib.cf_memset_blocks(_ptr(cache), _ptr(block_ids), block_ids.shape[0], _block_bytes(cache),
+                               cache.shape[0], _stream(cache)),
+          "cf_memset_blocks")
+
+
+def compaction_plan(used: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Host planner: moves that pack live blocks below num_used without overlap."""
+    lib = _lib.load()
+    u = np.ascontiguousarray(used, dtype=np.uint8)
+    n = u.shape[0]
+    src = np.empty(max(n, 1), dtype=np.int32)
+    dst = np.empty(max(n, 1), dtype=np.int32)
+    cnt = ctypes.c_int32(0)
+    check(lib.cf_compaction_plan(u.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), n,
+                                 src.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                 dst.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                 ctypes.byref(cnt)),
+          "cf_compaction_plan")
+    return src[: cnt.value].copy(), dst[: cnt.value].copy()
+
+
+def check_compaction_plan(src: np.ndarray, dst: np.ndarray, num_blocks: int) -> int:
+    """Returns the cf_status of the host-side race check (CF_OK, CF_ERR_PLAN, ...)."""
+    lib = _lib.load()
+    s = np.ascontiguousarray(src, dtype=np.int32)
+    d = np.ascontiguousarray(dst, dtype=np.int32)
+    return int(lib.cf_check_compaction_plan(s.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                            d.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                            s.shape[0], int(num_blocks)))
+
+
+def device_errors(device: int = 0, clear: bool = True) -> int:
+    """OR of CF_DEVERR_* bits recorded by kernels on `device` (synchronises it)."""
+    lib = _lib.load()
+    bits = ctypes.c_uint32(0)
+    check(lib.cf_get_device_errors(int(device), ctypes.byref(bits), 1 if clear else 0),
+          "cf_get_device_errors")
+    return int(bits.value)

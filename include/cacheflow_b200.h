@@ -1,0 +1,202 @@
+/*
+ * cacheflow_b200.h -- C ABI of the B200 (sm_100a) KV-cache kernel layer.
+ *
+ * Every entry point is a drop-in for one operator of CacheFlow's CUDA layer
+ * (src/cacheflow/cuda/*.cuh in the CacheFlow sources); the comment above each
+ * declaration names the reference interface it replaces (file:line).
+ *
+ * Conventions shared by all entry points:
+ *   - All tensor pointers are DEVICE pointers unless a comment says otherwise;
+ *     the caller owns every buffer and no entry point allocates device memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call is asynchronous on that stream and re-entrant.
+ *   - Host-visible arguments are validated before any launch; a bad argument
+ *     returns CF_ERR_INVALID_ARGUMENT and launches nothing.  Values that only
+ *     the device can see (block ids, slots, context lengths) are range-checked
+ *     inside the kernels: a bad value is skipped and recorded in a per-device
+ *     error word that cf_get_device_errors() reads.  No kernel traps.
+ *   - Cache layout (both K and V):  [num_blocks, num_kv_heads, block_size,
+ *     head_dim], contiguous, element type `dtype` (CacheFlow's layout,
+ *     paged_attention.cuh:27-28).
+ */
+#ifndef CACHEFLOW_B200_H_
+#define CACHEFLOW_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CF_API __attribute__((visibility("default")))
+#else
+#define CF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CF_ABI_VERSION 1
+
+typedef enum cf_status {
+  CF_OK = 0,
+  CF_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad shape     */
+  CF_ERR_UNSUPPORTED = 2,      /* no kernel for this head_dim/block_size/dtype */
+  CF_ERR_WORKSPACE = 3,        /* caller-provided scratch is too small       */
+  CF_ERR_CUDA = 4,             /* a CUDA runtime call failed; see cf_last_cuda_error() */
+  CF_ERR_PLAN = 5              /* a block-move plan would race (overlapping src/dst) */
+} cf_status;
+
+typedef enum cf_dtype {
+  CF_F32 = 0,  /* float  (the reference's only type) */
+  CF_F16 = 1,  /* IEEE half                          */
+  CF_BF16 = 2  /* bfloat16                           */
+} cf_dtype;
+
+/* Bits of the per-device error word (cf_get_device_errors). */
+#define CF_DEVERR_BLOCK_ID 0x1u    /* block-table / pair entry outside [0, num_blocks) */
+#define CF_DEVERR_SLOT 0x2u        /* slot_mapping entry outside the pool              */
+#define CF_DEVERR_CONTEXT_LEN 0x4u /* context length < 0 or > max_blocks_per_seq*bs   */
+#define CF_DEVERR_TIMEOUT 0x8u     /* a bounded pipeline wait gave up (kernel returned) */
+
+/* Parameters of one paged decode-attention call.  Same fields and meaning as
+ * cacheflow::cuda::PagedAttentionParams (paged_attention.cuh:25-40) plus
+ * `num_blocks` (pool size, used to range-check block ids; 0 = unchecked) and
+ * `dtype` (type of query, caches and output). */
+typedef struct cf_paged_attention_params {
+  const void* query;            /* [num_seqs, num_heads, head_dim]            */
+  const void* key_cache;        /* [num_blocks, num_kv_heads, block_size, head_dim] */
+  const void* value_cache;      /* same layout as key_cache                   */
+  void* output;                 /* [num_seqs, num_heads, head_dim]            */
+  const int32_t* block_tables;  /* [num_seqs, max_blocks_per_seq]            */
+  const int32_t* context_lens;  /* [num_seqs]                                 */
+  float scale;                  /* softmax scale, usually 1/sqrt(head_dim)    */
+  int32_t num_seqs;
+  int32_t num_heads;
+  int32_t num_kv_heads;         /* num_heads % num_kv_heads == 0 (GQA/MQA)    */
+  int32_t head_dim;             /* 64, 128 or 256                             */
+  int32_t block_size;           /* tokens per KV block: 16                    */
+  int32_t max_context_len;      /* host-side upper bound of context_lens      */
+  int32_t max_blocks_per_seq;   /* row stride of block_tables                 */
+  int64_t num_blocks;           /* pool size; 0 = do not range-check ids      */
+  int32_t dtype;                /* cf_dtype                                   */
+} cf_paged_attention_params;
+
+/* Decode attention, one query token per sequence.
+ * Replaces cacheflow::cuda::launch_paged_attention_v1 (paged_attention.cuh:44-46).
+ * `workspace` is optional: with NULL the whole context of a (sequence, KV head)
+ * is handled by one CTA; with at least cf_paged_attention_v1_workspace_size()
+ * bytes the context is split across CTAs and merged by a second kernel. */
+CF_API cf_status cf_paged_attention_v1(const cf_paged_attention_params* params,
+                                void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* Bytes of workspace the split path of cf_paged_attention_v1 uses for these
+ * params (depends only on host-side fields); 0 means it never splits. */
+CF_API size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* params);
+
+/* Partitioned decode attention: partitions of 512 tokens, then an exp-sum/max
+ * reduce kernel.  Replaces cacheflow::cuda::launch_paged_attention_v2
+ * (paged_attention.cuh:48-54).  exp_sums/max_logits are
+ * [num_seqs, num_heads, num_partitions] and tmp_output is
+ * [num_seqs, num_heads, num_partitions, head_dim], all float32.  They are
+ * overwritten (no pre-zeroing needed) and hold, per partition: the max logit,
+ * the sum of exp(logit - max) and the partition's normalised output.
+ * num_partitions must be >= ceil(max_context_len / 512). */
+CF_API cf_status cf_paged_attention_v2(const cf_paged_attention_params* params,
+                                float* exp_sums, float* max_logits,
+                                float* tmp_output, int32_t num_partitions,
+                                void* stream);
+
+/* Scatter new K/V rows into their cache slots:
+ *   cache[slot / block_size, h, slot % block_size, :] = kv[t, h, :]
+ * with slot = slot_mapping[t].  A negative slot skips the token (padding).
+ * Replaces cacheflow::cuda::launch_reshape_and_cache (kv_cache_kernels.cuh:17-27). */
+CF_API cf_status cf_reshape_and_cache(const void* key, const void* value,
+                               void* key_cache, void* value_cache,
+                               const int32_t* slot_mapping, int32_t num_tokens,
+                               int32_t num_kv_heads, int32_t head_dim,
+                               int32_t block_size, int64_t num_blocks,
+                               int32_t dtype, void* stream);
+
+/* Copy whole K and V blocks within one cache (copy-on-write forks):
+ * for each pair i, block block_mapping[2i+1] := block block_mapping[2i].
+ * Pairs run concurrently: a destination must not be another pair's source.
+ * Replaces cacheflow::cuda::launch_copy_blocks (kv_cache_kernels.cuh:29-37). */
+CF_API cf_status cf_copy_blocks(void* key_cache, void* value_cache,
+                         const int64_t* block_mapping, int32_t num_pairs,
+                         int32_t num_kv_heads, int32_t head_dim,
+                         int32_t block_size, int64_t num_blocks, int32_t dtype,
+                         void* stream);
+
+/* Copy blocks of `block_size_bytes` between two caches, one of which may be
+ * pinned host memory (device <-> host swap): for each pair i, block
+ * block_mapping[2i+1] of dst_cache := block block_mapping[2i] of src_cache.
+ * block_mapping is device-readable (device or pinned host).  Runs on the SMs
+ * through the host link, like the reference.
+ * Replaces cacheflow::cuda::launch_swap_blocks (kv_cache_kernels.cuh:39-45). */
+CF_API cf_status cf_swap_blocks(const void* src_cache, void* dst_cache,
+                         const int64_t* block_mapping, int32_t num_pairs,
+                         int64_t block_size_bytes, void* stream);
+
+/* Same copy as cf_swap_blocks, with block_mapping in HOST memory: pairs whose
+ * source and destination ids both advance by one are merged into one
+ * cudaMemcpyAsync, so the copy engines move them (no SM time).  Use a side
+ * stream so the swap overlaps attention. */
+CF_API cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
+                             const int64_t* host_block_mapping,
+                             int32_t num_pairs, int64_t block_size_bytes,
+                             void* stream);
+
+/* In-place defragmentation: for each i, K and V block dst_ids[i] := block
+ * src_ids[i] (src == dst is skipped).  All moves run concurrently, so the
+ * plan must not overlap: no destination may also be a source, and no
+ * destination may repeat (cf_compaction_plan builds such plans and
+ * cf_check_compaction_plan verifies one on the host).
+ * Replaces cacheflow::cuda::launch_compact_kv_cache (kv_cache_kernels.cuh:47-56). */
+CF_API cf_status cf_compact_kv_cache(void* key_cache, void* value_cache,
+                              const int32_t* src_block_ids,
+                              const int32_t* dst_block_ids, int32_t num_moves,
+                              int32_t num_kv_heads, int32_t head_dim,
+                              int32_t block_size, int64_t num_blocks,
+                              int32_t dtype, void* stream);
+
+/* Zero the listed blocks of one cache (blocks of block_size_bytes bytes).
+ * Replaces cacheflow::cuda::launch_memset_blocks (memory_utils.cuh:28-33). */
+CF_API cf_status cf_memset_blocks(void* cache, const int32_t* block_ids,
+                           int32_t num_listed, int64_t block_size_bytes,
+                           int64_t num_blocks, void* stream);
+
+/* HOST-side planner for compaction.  `used` has num_blocks bytes (non-zero =
+ * block holds live data).  Emits moves that pack the live blocks into
+ * [0, num_used): every live block at or above num_used moves into a free slot
+ * below it, so sources and destinations never overlap.  `src_out`/`dst_out`
+ * need room for num_blocks entries; *num_moves receives the count.
+ * Pure host code; counterpart of the planning CacheFlow leaves to
+ * BlockManager::compute_fragmentation (block_manager.cpp:177-222). */
+CF_API cf_status cf_compaction_plan(const uint8_t* used, int64_t num_blocks,
+                             int32_t* src_out, int32_t* dst_out,
+                             int32_t* num_moves);
+
+/* HOST-side check that a compaction / copy plan is race-free: ids in range,
+ * destinations unique, and no destination also used as a source.
+ * Returns CF_OK, CF_ERR_INVALID_ARGUMENT (out of range) or CF_ERR_PLAN. */
+CF_API cf_status cf_check_compaction_plan(const int32_t* src_ids, const int32_t* dst_ids,
+                                   int32_t num_moves, int64_t num_blocks);
+
+/* Reads (and optionally clears) the OR of all device error bits recorded by
+ * kernels on `device` since the last clear.  Synchronises that device. */
+CF_API cf_status cf_get_device_errors(int32_t device, uint32_t* flags, int32_t clear);
+
+/* The last cudaError_t seen by any entry point on this thread. */
+CF_API int32_t cf_last_cuda_error(void);
+
+CF_API const char* cf_status_string(cf_status status);
+
+/* CF_ABI_VERSION of the loaded library. */
+CF_API int32_t cf_abi_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* CACHEFLOW_B200_H_ */

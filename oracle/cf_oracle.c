@@ -1,0 +1,271 @@
+/*
+ * cf_oracle.c -- CPU restatement of CacheFlow's KV-cache kernel path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker; see cf_oracle.h).  Nothing in the
+ * product links or calls this file.
+ *
+ * Reference lines followed (CacheFlow, src/cacheflow/cuda/):
+ *   paged_attention.cuh:25-31   operand layouts
+ *   paged_attention.cu:58        kv head = h / (num_heads / num_kv_heads)
+ *   paged_attention.cu:75-83     block walk over block_tables, stop at ctx
+ *   paged_attention.cu:85-87     K row index ((phys*Hkv + kvh)*bs + off)*D
+ *   paged_attention.cu:151-153   V row index (same)
+ *   paged_attention.cu:203-205   v2 partition = tokens [p*P, min((p+1)*P, ctx))
+ *   paged_attention.cu:313-329   v2 reduce (restated with correct LSE weights)
+ *   kv_cache_kernels.cu:34-42    slot -> (slot / bs, slot % bs) scatter
+ *   kv_cache_kernels.cu:71-83    copy_blocks pairs (src, dst) = mapping[2i], [2i+1]
+ *   kv_cache_kernels.cu:111-118  swap_blocks pairs, same layout
+ *   kv_cache_kernels.cu:150-164  compact moves src_ids[i] -> dst_ids[i], skip src==dst
+ *   memory_utils.cu:46-57        memset_blocks
+ */
+#include "cf_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+static double half_bits_to_double(uint16_t h) {
+  const int sign = (h >> 15) & 1;
+  const int exp = (h >> 10) & 0x1f;
+  const int man = h & 0x3ff;
+  double v;
+  if (exp == 0)
+    v = ldexp((double)man, -24); /* subnormal */
+  else if (exp == 31)
+    v = man ? NAN : INFINITY;
+  else
+    v = ldexp((double)(man | 0x400), exp - 25);
+  return sign ? -v : v;
+}
+
+static double bf16_bits_to_double(uint16_t b) {
+  uint32_t w = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &w, sizeof f);
+  return (double)f;
+}
+
+double cfo_load(const void* base, int64_t index, int32_t dtype) {
+  switch (dtype) {
+    case 0: return (double)((const float*)base)[index];
+    case 1: return half_bits_to_double(((const uint16_t*)base)[index]);
+    default: return bf16_bits_to_double(((const uint16_t*)base)[index]);
+  }
+}
+
+/* ---------------------------------------------------------------- attention */
+
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  double* out;
+  const int32_t* tables;
+  const int32_t* ctx;
+  double scale;
+  int32_t S, H, Hkv, D, bs, mbps, dtype;
+  int32_t next; /* next (seq, head) pair, taken under `mu` */
+  pthread_mutex_t mu;
+} attn_job;
+
+/* Logits of query head h of sequence s over tokens [t0, t1), into `sc`. */
+static void logits(const attn_job* j, int s, int h, int t0, int t1, double* sc) {
+  const int kvh = h / (j->H / j->Hkv);
+  const int64_t qoff = ((int64_t)s * j->H + h) * j->D;
+  for (int t = t0; t < t1; ++t) {
+    const int blk = t / j->bs, off = t % j->bs;
+    const int64_t phys = j->tables[(int64_t)s * j->mbps + blk];
+    const int64_t koff = ((phys * j->Hkv + kvh) * j->bs + off) * j->D;
+    double dot = 0.0;
+    for (int d = 0; d < j->D; ++d)
+      dot += cfo_load(j->q, qoff + d, j->dtype) * cfo_load(j->k, koff + d, j->dtype);
+    sc[t - t0] = dot * j->scale;
+  }
+}
+
+/* Softmax-weighted V over [t0, t1) given logits; writes o[D] and returns
+ * (max, sum exp(logit - max)) through *m, *l.  Empty range: o = 0, l = 0. */
+static void weighted_v(const attn_job* j, int s, int h, int t0, int t1, double* sc, double* o,
+                       double* m, double* l) {
+  const int kvh = h / (j->H / j->Hkv);
+  double mx = -INFINITY, sum = 0.0;
+  for (int d = 0; d < j->D; ++d) o[d] = 0.0;
+  for (int t = t0; t < t1; ++t) mx = sc[t - t0] > mx ? sc[t - t0] : mx;
+  for (int t = t0; t < t1; ++t) {
+    const double w = exp(sc[t - t0] - mx);
+    sum += w;
+    const int blk = t / j->bs, off = t % j->bs;
+    const int64_t phys = j->tables[(int64_t)s * j->mbps + blk];
+    const int64_t voff = ((phys * j->Hkv + kvh) * j->bs + off) * j->D;
+    for (int d = 0; d < j->D; ++d) o[d] += w * cfo_load(j->v, voff + d, j->dtype);
+  }
+  if (sum > 0)
+    for (int d = 0; d < j->D; ++d) o[d] /= sum;
+  *m = mx;
+  *l = sum;
+}
+
+static void* attn_worker(void* arg) {
+  attn_job* j = (attn_job*)arg;
+  int cap = 0;
+  double* sc = NULL;
+  for (;;) {
+    pthread_mutex_lock(&j->mu);
+    const int idx = j->next++;
+    pthread_mutex_unlock(&j->mu);
+    if (idx >= j->S * j->H) break;
+    const int s = idx / j->H, h = idx % j->H;
+    const int ctx = j->ctx[s];
+    if (ctx > cap) {
+      free(sc);
+      cap = ctx;
+      sc = (double*)malloc(sizeof(double) * (size_t)cap);
+    }
+    double m, l;
+    logits(j, s, h, 0, ctx, sc);
+    weighted_v(j, s, h, 0, ctx, sc, j->out + ((int64_t)s * j->H + h) * j->D, &m, &l);
+  }
+  free(sc);
+  return NULL;
+}
+
+void cfo_paged_attention(const void* query, const void* key_cache, const void* value_cache,
+                         double* out, const int32_t* block_tables, const int32_t* context_lens,
+                         float scale, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t block_size, int32_t max_blocks_per_seq,
+                         int32_t dtype, int32_t num_threads) {
+  attn_job j = {query, key_cache, value_cache, out, block_tables, context_lens, (double)scale,
+                num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
+                dtype, 0};
+  pthread_mutex_init(&j.mu, NULL);
+  if (num_threads <= 1) {
+    attn_worker(&j);
+  } else {
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)num_threads);
+    for (int i = 0; i < num_threads; ++i) pthread_create(&th[i], NULL, attn_worker, &j);
+    for (int i = 0; i < num_threads; ++i) pthread_join(th[i], NULL);
+    free(th);
+  }
+  pthread_mutex_destroy(&j.mu);
+}
+
+void cfo_paged_attention_partitions(const void* query, const void* key_cache,
+                                    const void* value_cache, const int32_t* block_tables,
+                                    const int32_t* context_lens, float scale, int32_t num_seqs,
+                                    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                    int32_t block_size, int32_t max_blocks_per_seq, int32_t dtype,
+                                    int32_t partition_size, int32_t num_partitions,
+                                    double* max_logits, double* exp_sums, double* tmp_out) {
+  attn_job j = {query, key_cache, value_cache, NULL, block_tables, context_lens, (double)scale,
+                num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
+                dtype, 0};
+  double* sc = (double*)malloc(sizeof(double) * (size_t)(partition_size > 0 ? partition_size : 1));
+  for (int s = 0; s < num_seqs; ++s) {
+    const int ctx = context_lens[s];
+    for (int h = 0; h < num_heads; ++h) {
+      for (int p = 0; p < num_partitions; ++p) {
+        const int t0 = p * partition_size;
+        if (t0 >= ctx) break;
+        const int t1 = t0 + partition_size < ctx ? t0 + partition_size : ctx;
+        const int64_t flat = ((int64_t)s * num_heads + h) * num_partitions + p;
+        logits(&j, s, h, t0, t1, sc);
+        weighted_v(&j, s, h, t0, t1, sc, tmp_out + flat * head_dim, &max_logits[flat],
+                   &exp_sums[flat]);
+      }
+    }
+  }
+  free(sc);
+}
+
+void cfo_paged_attention_reduce(const double* max_logits, const double* exp_sums,
+                                const double* tmp_out, const int32_t* context_lens,
+                                int32_t num_seqs, int32_t num_heads, int32_t head_dim,
+                                int32_t partition_size, int32_t num_partitions, double* out) {
+  for (int s = 0; s < num_seqs; ++s) {
+    const int ctx = context_lens[s];
+    int parts = (ctx + partition_size - 1) / partition_size;
+    if (parts > num_partitions) parts = num_partitions;
+    for (int h = 0; h < num_heads; ++h) {
+      const int64_t base = ((int64_t)s * num_heads + h) * num_partitions;
+      double* o = out + ((int64_t)s * num_heads + h) * head_dim;
+      double M = -INFINITY, L = 0.0;
+      for (int p = 0; p < parts; ++p) M = max_logits[base + p] > M ? max_logits[base + p] : M;
+      for (int d = 0; d < head_dim; ++d) o[d] = 0.0;
+      for (int p = 0; p < parts; ++p) {
+        const double w = exp_sums[base + p] * exp(max_logits[base + p] - M);
+        L += w;
+        for (int d = 0; d < head_dim; ++d) o[d] += w * tmp_out[(base + p) * head_dim + d];
+      }
+      if (L > 0)
+        for (int d = 0; d < head_dim; ++d) o[d] /= L;
+    }
+  }
+}
+
+/* ------------------------------------------------------------- cache moves */
+
+void cfo_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                           void* value_cache, const int32_t* slot_mapping, int32_t num_tokens,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                           int32_t elem_bytes) {
+  const int64_t row = (int64_t)head_dim * elem_bytes;
+  for (int t = 0; t < num_tokens; ++t) {
+    const int64_t slot = slot_mapping[t];
+    if (slot < 0) continue; /* padding token */
+    const int64_t blk = slot / block_size, off = slot % block_size;
+    for (int h = 0; h < num_kv_heads; ++h) {
+      const int64_t src = ((int64_t)t * num_kv_heads + h) * row;
+      const int64_t dst = ((blk * num_kv_heads + h) * block_size + off) * row;
+      memcpy((char*)key_cache + dst, (const char*)key + src, (size_t)row);
+      memcpy((char*)value_cache + dst, (const char*)value + src, (size_t)row);
+    }
+  }
+}
+
+void cfo_copy_blocks(void* key_cache, void* value_cache, const int64_t* block_mapping,
+                     int32_t num_pairs, int64_t block_bytes) {
+  for (int i = 0; i < num_pairs; ++i) {
+    const int64_t s = block_mapping[2 * i], d = block_mapping[2 * i + 1];
+    memmove((char*)key_cache + d * block_bytes, (char*)key_cache + s * block_bytes,
+            (size_t)block_bytes);
+    memmove((char*)value_cache + d * block_bytes, (char*)value_cache + s * block_bytes,
+            (size_t)block_bytes);
+  }
+}
+
+void cfo_swap_blocks(const void* src_cache, void* dst_cache, const int64_t* block_mapping,
+                     int32_t num_pairs, int64_t block_bytes) {
+  for (int i = 0; i < num_pairs; ++i) {
+    const int64_t s = block_mapping[2 * i], d = block_mapping[2 * i + 1];
+    memcpy((char*)dst_cache + d * block_bytes, (const char*)src_cache + s * block_bytes,
+           (size_t)block_bytes);
+  }
+}
+
+/* All sources are read before any destination is written (parallel
+ * assignment), which is what the concurrent reference kernel produces for
+ * every plan whose destinations are not also sources. */
+void cfo_compact_kv_cache(void* key_cache, void* value_cache, const int32_t* src_ids,
+                          const int32_t* dst_ids, int32_t num_moves, int64_t block_bytes) {
+  void* caches[2] = {key_cache, value_cache};
+  char* stage = (char*)malloc((size_t)(num_moves > 0 ? num_moves : 1) * (size_t)block_bytes);
+  for (int c = 0; c < 2; ++c) {
+    char* base = (char*)caches[c];
+    for (int i = 0; i < num_moves; ++i)
+      memcpy(stage + (int64_t)i * block_bytes, base + (int64_t)src_ids[i] * block_bytes,
+             (size_t)block_bytes);
+    for (int i = 0; i < num_moves; ++i) {
+      if (src_ids[i] == dst_ids[i]) continue;
+      memcpy(base + (int64_t)dst_ids[i] * block_bytes, stage + (int64_t)i * block_bytes,
+             (size_t)block_bytes);
+    }
+  }
+  free(stage);
+}
+
+void cfo_memset_blocks(void* cache, const int32_t* block_ids, int32_t num_listed,
+                       int64_t block_bytes) {
+  for (int i = 0; i < num_listed; ++i)
+    memset((char*)cache + (int64_t)block_ids[i] * block_bytes, 0, (size_t)block_bytes);
+}

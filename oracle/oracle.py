@@ -1,0 +1,237 @@
+"""Python access to the CPU oracle (cf_oracle.c) and to the reference-derived
+libraries under oracle/_ref/.
+
+TEST / BENCH INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke()
+and the CPU-baseline leg of bench.py as the checker.  The product package
+(cacheflow_b200) never imports this module.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, c_double, c_float, c_int32, c_int64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "libcf_oracle.so"
+REF_CUDA_LIB = HERE / "_ref" / "libcf_ref_cuda.so"
+REF_CPU_LIB = HERE / "_ref" / "libcf_ref_cpu.so"
+
+DTYPE_CODE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1}
+BF16 = 2  # numpy has no bfloat16: bf16 arrays are carried as uint16 bit patterns
+
+
+def build(with_reference: bool | None = None) -> None:
+    """Builds the oracle (and, when the reference checkout exists, oracle/_ref)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "libcf_oracle.so"], check=True)
+    ref = os.environ.get("CF_REFERENCE_DIR", "/root/reference")
+    if with_reference is None:
+        with_reference = Path(ref, "src", "cacheflow").is_dir()
+    if with_reference:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
+
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not ORACLE_LIB.exists():
+            build(with_reference=False)
+        L = ctypes.CDLL(str(ORACLE_LIB))
+        L.cfo_paged_attention.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_float] + [c_int32] * 8
+        L.cfo_paged_attention_partitions.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                                     c_float] + [c_int32] * 9 + [c_void_p] * 3
+        L.cfo_paged_attention_reduce.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int32] * 5 + [c_void_p]
+        L.cfo_reshape_and_cache.argtypes = [c_void_p] * 5 + [c_int32] * 5
+        L.cfo_copy_blocks.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_swap_blocks.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_compact_kv_cache.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_memset_blocks.argtypes = [c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_load.restype = c_double
+        L.cfo_load.argtypes = [c_void_p, c_int64, c_int32]
+        _LIB = L
+    return _LIB
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags.c_contiguous
+    return a.ctypes.data
+
+
+def _code(a: np.ndarray, dtype_code: int | None) -> int:
+    if dtype_code is not None:
+        return dtype_code
+    return DTYPE_CODE[a.dtype]
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, context_lens, scale, dtype_code=None,
+                    num_threads=1) -> np.ndarray:
+    """float64 [S, H, D] attention output (the intended softmax attention)."""
+    S, H, D = q.shape
+    _, Hkv, bs, _ = k_cache.shape
+    out = np.zeros((S, H, D), dtype=np.float64)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    cl = np.ascontiguousarray(context_lens, dtype=np.int32)
+    lib().cfo_paged_attention(_p(q), _p(k_cache), _p(v_cache), _p(out), _p(bt), _p(cl), float(scale),
+                              S, H, Hkv, D, bs, bt.shape[1], _code(q, dtype_code), num_threads)
+    return out
+
+
+def paged_attention_partitions(q, k_cache, v_cache, block_tables, context_lens, scale,
+                               partition_size, num_partitions, dtype_code=None):
+    S, H, D = q.shape
+    _, Hkv, bs, _ = k_cache.shape
+    mx = np.full((S, H, num_partitions), np.nan)
+    es = np.full((S, H, num_partitions), np.nan)
+    to = np.full((S, H, num_partitions, D), np.nan)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    cl = np.ascontiguousarray(context_lens, dtype=np.int32)
+    lib().cfo_paged_attention_partitions(_p(q), _p(k_cache), _p(v_cache), _p(bt), _p(cl), float(scale),
+                                         S, H, Hkv, D, bs, bt.shape[1], _code(q, dtype_code),
+                                         partition_size, num_partitions, _p(mx), _p(es), _p(to))
+    return mx, es, to
+
+
+def paged_attention_reduce(mx, es, to, context_lens, partition_size) -> np.ndarray:
+    S, H, P, D = to.shape
+    out = np.zeros((S, H, D))
+    cl = np.ascontiguousarray(context_lens, dtype=np.int32)
+    lib().cfo_paged_attention_reduce(_p(np.ascontiguousarray(mx)), _p(np.ascontiguousarray(es)),
+                                     _p(np.ascontiguousarray(to)), _p(cl), S, H, D, partition_size,
+                                     P, _p(out))
+    return out
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping) -> None:
+    """In place on key_cache / value_cache (numpy, any dtype)."""
+    T, Hkv, D = key.shape
+    bs = key_cache.shape[2]
+    sm = np.ascontiguousarray(slot_mapping, dtype=np.int32)
+    lib().cfo_reshape_and_cache(_p(key), _p(value), _p(key_cache), _p(value_cache), _p(sm), T, Hkv, D,
+                                bs, key.itemsize)
+
+
+def copy_blocks(key_cache, value_cache, block_mapping) -> None:
+    m = np.ascontiguousarray(block_mapping, dtype=np.int64)
+    lib().cfo_copy_blocks(_p(key_cache), _p(value_cache), _p(m), m.shape[0],
+                          key_cache[0].nbytes)
+
+
+def swap_blocks(src, dst, block_mapping) -> None:
+    m = np.ascontiguousarray(block_mapping, dtype=np.int64)
+    lib().cfo_swap_blocks(_p(src), _p(dst), _p(m), m.shape[0], src[0].nbytes)
+
+
+def compact_kv_cache(key_cache, value_cache, src_ids, dst_ids) -> None:
+    s = np.ascontiguousarray(src_ids, dtype=np.int32)
+    d = np.ascontiguousarray(dst_ids, dtype=np.int32)
+    lib().cfo_compact_kv_cache(_p(key_cache), _p(value_cache), _p(s), _p(d), s.shape[0],
+                               key_cache[0].nbytes)
+
+
+def memset_blocks(cache, block_ids) -> None:
+    b = np.ascontiguousarray(block_ids, dtype=np.int32)
+    lib().cfo_memset_blocks(_p(cache), _p(b), b.shape[0], cache[0].nbytes)
+
+
+# ---------------------------------------------------------------------------
+# numpy restatement of the attention math (independent second restatement,
+# used to cross-check the C oracle on small cases).
+# ---------------------------------------------------------------------------
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def to_f64(a: np.ndarray, dtype_code: int | None = None) -> np.ndarray:
+    if dtype_code == BF16:
+        return bf16_bits_to_f32(a).astype(np.float64)
+    return a.astype(np.float64)
+
+
+def paged_attention_numpy(q, k_cache, v_cache, block_tables, context_lens, scale, dtype_code=None):
+    qd, kd, vd = (to_f64(x, dtype_code) for x in (q, k_cache, v_cache))
+    S, H, D = q.shape
+    Hkv, bs = k_cache.shape[1], k_cache.shape[2]
+    out = np.zeros((S, H, D))
+    for s in range(S):
+        ctx = int(context_lens[s])
+        if ctx == 0:
+            continue
+        t = np.arange(ctx)
+        phys = np.asarray(block_tables[s])[t // bs]
+        for h in range(H):
+            kvh = h // (H // Hkv)
+            K = kd[phys, kvh, t % bs]
+            V = vd[phys, kvh, t % bs]
+            sc = (K @ qd[s, h]) * np.float64(np.float32(scale))
+            w = np.exp(sc - sc.max())
+            out[s, h] = (w @ V) / w.sum()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Reference-derived libraries (built from the reference sources by Makefile).
+# ---------------------------------------------------------------------------
+class RefCuda:
+    """CacheFlow's own CUDA kernels (fp32), for GPU-side comparison."""
+
+    def __init__(self):
+        if not REF_CUDA_LIB.exists():
+            raise FileNotFoundError(f"{REF_CUDA_LIB} not built (make -C oracle ref)")
+        L = ctypes.CDLL(str(REF_CUDA_LIB), mode=os.RTLD_LOCAL)
+        L.ref_paged_attention_v1.argtypes = [c_void_p] * 6 + [c_float] + [c_int32] * 7
+        L.ref_reshape_and_cache.argtypes = [c_void_p] * 5 + [c_int32] * 4
+        L.ref_copy_blocks.argtypes = [c_void_p] * 3 + [c_int32] * 4
+        L.ref_swap_blocks.argtypes = [c_void_p] * 3 + [c_int32] * 2
+        L.ref_compact_kv_cache.argtypes = [c_void_p] * 4 + [c_int32] * 4
+        L.ref_memset_blocks.argtypes = [c_void_p] * 2 + [c_int32] * 2
+        self.lib = L
+
+
+class RefCpu:
+    """CacheFlow's own CPU decode step (batch_decode.cpp:190-240), fp32 only."""
+
+    def __init__(self, num_heads, num_kv_heads, head_dim, num_blocks, num_threads):
+        if not REF_CPU_LIB.exists():
+            raise FileNotFoundError(f"{REF_CPU_LIB} not built (make -C oracle ref)")
+        L = ctypes.CDLL(str(REF_CPU_LIB), mode=os.RTLD_LOCAL)
+        L.refcpu_create.restype = c_void_p
+        L.refcpu_create.argtypes = [c_int32, c_int32, c_int32, c_int64, c_int32]
+        L.refcpu_key_cache.restype = c_void_p
+        L.refcpu_key_cache.argtypes = [c_void_p]
+        L.refcpu_value_cache.restype = c_void_p
+        L.refcpu_value_cache.argtypes = [c_void_p]
+        L.refcpu_set_batch.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_int32]
+        L.refcpu_step.restype = c_double
+        L.refcpu_step.argtypes = [c_void_p]
+        L.refcpu_destroy.argtypes = [c_void_p]
+        self.lib = L
+        self.shape = (num_blocks, num_kv_heads, 16, head_dim)
+        self.h = L.refcpu_create(num_heads, num_kv_heads, head_dim, num_blocks, num_threads)
+        self.num_threads = num_threads
+
+    def caches(self) -> tuple[np.ndarray, np.ndarray]:
+        n = int(np.prod(self.shape))
+        k = np.ctypeslib.as_array(ctypes.cast(self.lib.refcpu_key_cache(self.h), POINTER(c_float)), (n,))
+        v = np.ctypeslib.as_array(ctypes.cast(self.lib.refcpu_value_cache(self.h), POINTER(c_float)), (n,))
+        return k.reshape(self.shape), v.reshape(self.shape)
+
+    def set_batch(self, context_lens: np.ndarray, block_tables: np.ndarray) -> None:
+        self._cl = np.ascontiguousarray(context_lens, dtype=np.int32)
+        self._bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+        self.lib.refcpu_set_batch(self.h, self._cl.shape[0], _p(self._cl), _p(self._bt), self._bt.shape[1])
+
+    def step(self) -> float:
+        return float(self.lib.refcpu_step(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.refcpu_destroy(self.h)
+            self.h = None

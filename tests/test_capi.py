@@ -1,0 +1,145 @@
+"""CPU-side checks of the drop-in boundary: the library loads, exports exactly
+what include/*.h declares, rejects bad arguments before touching the GPU, and
+its host-only planners behave.  No compute calls (there is no GPU here)."""
+
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared_c_functions():
+    text = (ROOT / "include" / "cacheflow_b200.h").read_text()
+    return re.findall(r"CF_API\s+[\w\s\*]+?\b(cf_\w+)\s*\(", text)
+
+
+def _exports(lib_path):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lib_path)], capture_output=True, text=True,
+                         check=True).stdout
+    names = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    demangled = subprocess.run(["c++filt"], input="\n".join(sorted(names)), capture_output=True, text=True,
+                               check=True).stdout.splitlines()
+    return names, set(demangled)
+
+
+def test_library_exports_every_declared_c_function(cflib):
+    from cacheflow_b200 import _lib
+
+    declared = set(_declared_c_functions())
+    assert declared == set(_lib.SIGNATURES), "ctypes binding and header disagree"
+    names, _ = _exports(_lib.LIB_PATH)
+    assert declared <= names
+    for n in declared:
+        assert getattr(cflib, n) is not None
+
+
+def test_library_exports_reference_cpp_entry_points(cflib):
+    from cacheflow_b200 import _lib
+
+    _, demangled = _exports(_lib.LIB_PATH)
+    for sym in _lib.COMPAT_SYMBOLS:
+        assert sym in demangled, sym
+    # nothing but the ABI is exported
+    extra = {d for d in demangled if not (d.startswith("cf_") or d.startswith("cacheflow::cuda::"))}
+    assert not extra, extra
+
+
+def test_compat_header_declares_reference_signatures():
+    """Every C++ entry point of the compat header is exported (same mangling as
+    CacheFlow's own declarations, checked below when its sources are present)."""
+    text = (ROOT / "include" / "cacheflow_b200_compat.hpp").read_text()
+    for fn in ["launch_paged_attention_v1", "launch_paged_attention_v2", "launch_reshape_and_cache",
+               "launch_copy_blocks", "launch_swap_blocks", "launch_compact_kv_cache", "launch_memset_blocks",
+               "get_gpu_free_memory", "async_memcpy_h2d", "synchronize_stream"]:
+        assert re.search(rf"CF_COMPAT_API\s+\w+\s+{fn}\(", text), fn
+
+
+REF = Path(os.environ.get("CF_REFERENCE_DIR", "/root/reference"))
+
+
+@pytest.mark.skipif(not (REF / "src" / "cacheflow").is_dir() or shutil.which("g++") is None,
+                    reason="CacheFlow sources not present")
+def test_reference_host_code_links_against_library(cflib, tmp_path):
+    """CacheFlow's own decode engine, compiled with CUDA enabled against its own
+    unchanged headers, links against libcacheflow_b200.so with no undefined
+    cacheflow::cuda symbol: the library is a drop-in for src/cacheflow/cuda/*.cu."""
+    from cacheflow_b200 import _lib
+
+    src = REF / "src"
+    out = tmp_path / "libengine.so"
+    cmd = ["g++", "-std=c++17", "-O1", "-fPIC", "-shared", "-DCACHEFLOW_USE_CUDA=1", f"-I{src}",
+           "-I/usr/local/cuda/include", str(src / "cacheflow/decode/batch_decode.cpp"),
+           str(src / "cacheflow/kv_cache/memory_pool.cpp"), "-o", str(out),
+           f"-L{_lib.LIB_PATH.parent}", "-lcacheflow_b200", "-Wl,--no-undefined",
+           "-L/usr/local/cuda/lib64", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
+    und = subprocess.run(["nm", "-D", "-C", "--undefined-only", str(out)], capture_output=True, text=True).stdout
+    used = [l for l in und.splitlines() if "cacheflow::cuda::" in l]
+    assert any("launch_paged_attention_v1" in l for l in used)
+    assert any("launch_paged_attention_v2" in l for l in used)
+
+
+def test_invalid_arguments_rejected_without_gpu(cflib):
+    from cacheflow_b200 import _lib
+
+    assert cflib.cf_abi_version() == 1
+    assert cflib.cf_paged_attention_v1(None, None, 0, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    p = _lib.AttentionParams()
+    p.num_seqs, p.num_heads, p.num_kv_heads, p.head_dim, p.block_size = 1, 6, 4, 128, 16
+    p.dtype = _lib.CF_BF16
+    assert cflib.cf_paged_attention_v1(ctypes.byref(p), None, 0, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    p.num_kv_heads, p.head_dim = 2, 96
+    assert cflib.cf_paged_attention_v1(ctypes.byref(p), None, 0, None) == _lib.CF_ERR_UNSUPPORTED
+    p.head_dim, p.block_size = 128, 32
+    assert cflib.cf_paged_attention_v1(ctypes.byref(p), None, 0, None) == _lib.CF_ERR_UNSUPPORTED
+    p.block_size, p.max_blocks_per_seq, p.max_context_len = 16, 2, 33  # 33 tokens > 2 blocks
+    assert cflib.cf_paged_attention_v1(ctypes.byref(p), None, 0, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    p.max_context_len, p.num_seqs = 10, 0  # empty batch is a no-op
+    assert cflib.cf_paged_attention_v1(ctypes.byref(p), None, 0, None) == _lib.CF_OK
+    p.num_seqs, p.max_context_len = 1, 600
+    p.query = p.key_cache = p.value_cache = p.output = p.block_tables = p.context_lens = 1 << 20
+    p.max_blocks_per_seq = 64
+    es = ctypes.c_void_p(1 << 20)
+    assert cflib.cf_paged_attention_v2(ctypes.byref(p), es, es, es, 1, None) == _lib.CF_ERR_WORKSPACE
+    assert cflib.cf_reshape_and_cache(None, None, None, None, None, 0, 8, 128, 16, 10, 2, None) == _lib.CF_OK
+    assert cflib.cf_reshape_and_cache(None, None, None, None, None, 4, 8, 128, 16, 10, 2, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_copy_blocks(None, None, None, -1, 8, 128, 16, 10, 2, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_swap_blocks(None, None, None, 3, 4096, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_compact_kv_cache(None, None, None, None, 0, 8, 128, 16, 10, 7, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_memset_blocks(None, None, 0, 4096, 10, None) == _lib.CF_OK
+    assert cflib.cf_status_string(_lib.CF_ERR_PLAN) == b"block-move plan would race"
+
+
+def test_compaction_planner_packs_without_overlap(cflib):
+    from cacheflow_b200 import _lib, ops
+
+    rng = np.random.default_rng(0)
+    for n, frac in [(1, 1.0), (10, 0.0), (1000, 0.5), (4096, 0.9), (777, 0.1)]:
+        used = rng.random(n) < frac
+        src, dst = ops.compaction_plan(used)
+        live = int(used.sum())
+        assert ops.check_compaction_plan(src, dst, n) == _lib.CF_OK
+        assert np.all(src >= live) and np.all(dst < live)
+        after = used.copy()
+        after[src] = False
+        after[dst] = True
+        assert after[:live].all() and not after[live:].any()
+
+
+def test_plan_checker_rejects_races(cflib):
+    from cacheflow_b200 import _lib, ops
+
+    assert ops.check_compaction_plan(np.array([5, 6]), np.array([1, 1]), 10) == _lib.CF_ERR_PLAN  # dup dst
+    assert ops.check_compaction_plan(np.array([5, 1]), np.array([1, 2]), 10) == _lib.CF_ERR_PLAN  # chain
+    assert ops.check_compaction_plan(np.array([5]), np.array([10]), 10) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert ops.check_compaction_plan(np.array([4, 4]), np.array([4, 7]), 10) == _lib.CF_OK  # self move skipped

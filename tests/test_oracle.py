@@ -1,0 +1,200 @@
+"""The CPU oracle checked on its own: against an independent numpy restatement,
+against the golden vectors recorded from CacheFlow's own kernels
+(tests/golden/), and for the algebraic identities the path relies on."""
+
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from cacheflow_b200 import workloads
+from cacheflow_b200.workloads import host_values
+from helpers import CODE, random_tables
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _case(rng, dtype, S, H, Hkv, D, ctx):
+    pool = sum((c + 15) // 16 for c in ctx) + 5
+    tables = random_tables(rng, ctx, pool)
+    q = host_values((S, H, D), dtype, 0.5, rng)
+    k = host_values((pool, Hkv, 16, D), dtype, 0.5, rng)
+    v = host_values((pool, Hkv, 16, D), dtype, 0.5, rng)
+    return q, k, v, tables, np.array(ctx, np.int32)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("H,Hkv,D", [(4, 4, 128), (8, 2, 64), (6, 3, 128)])
+def test_c_oracle_matches_numpy_restatement(oracle_mod, dtype, H, Hkv, D):
+    rng = np.random.default_rng(1)
+    ctx = [1, 15, 16, 17, 100, 300]
+    q, k, v, tables, cl = _case(rng, dtype, len(ctx), H, Hkv, D, ctx)
+    scale = 1 / math.sqrt(D)
+    a = oracle_mod.paged_attention(q, k, v, tables, cl, scale, CODE[dtype])
+    b = oracle_mod.paged_attention_numpy(q, k, v, tables, cl, scale, CODE[dtype])
+    np.testing.assert_allclose(a, b, rtol=1e-12, atol=1e-12)
+    a4 = oracle_mod.paged_attention(q, k, v, tables, cl, scale, CODE[dtype], num_threads=4)
+    assert np.array_equal(a, a4)
+
+
+def test_element_decoding(oracle_mod):
+    x = np.array([0.0, -1.5, 65504.0, 6.1e-5, 5.96e-8, np.inf], np.float16)
+    for i, val in enumerate(x):
+        assert oracle_mod.lib().cfo_load(x.ctypes.data, i, 1) == float(val)
+    f = np.array([1.0, -3.140625, 1e-20, 3.0e38], np.float32)
+    bits = (f.view(np.uint32) >> 16).astype(np.uint16)  # exact in bf16 for these values? truncate
+    for i in range(len(f)):
+        want = float((bits[i:i + 1].astype(np.uint32) << 16).view(np.float32)[0])
+        assert oracle_mod.lib().cfo_load(bits.ctypes.data, i, 2) == want
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5e-3], np.float32)  # ties and a normal value
+    bits = host_values_rounding(x)
+    import torch
+
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(bits, want)
+
+
+def host_values_rounding(x):
+    u = x.view(np.uint32)
+    r = ((u >> 16) & 1) + np.uint32(0x7FFF)
+    return ((u + r) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("P", [16, 64, 512])
+def test_partitions_then_reduce_equals_direct(oracle_mod, P):
+    rng = np.random.default_rng(2)
+    ctx = [1, P - 1, P, P + 1, 5 * P + 3]
+    q, k, v, tables, cl = _case(rng, "bf16", len(ctx), 8, 2, 128, ctx)
+    scale = 1 / math.sqrt(128)
+    nparts = (max(ctx) + P - 1) // P
+    mx, es, to = oracle_mod.paged_attention_partitions(q, k, v, tables, cl, scale, P, nparts, 2)
+    red = oracle_mod.paged_attention_reduce(mx, es, to, cl, P)
+    direct = oracle_mod.paged_attention(q, k, v, tables, cl, scale, 2)
+    np.testing.assert_allclose(red, direct, rtol=1e-12, atol=1e-13)
+
+
+def test_zero_context_is_zero(oracle_mod):
+    rng = np.random.default_rng(3)
+    q, k, v, tables, cl = _case(rng, "f32", 2, 2, 2, 64, [0, 5])
+    out = oracle_mod.paged_attention(q, k, v, tables, cl, 0.125, 0)
+    assert np.all(out[0] == 0) and np.all(np.isfinite(out[1]))
+
+
+def test_cache_ops_match_numpy(oracle_mod):
+    rng = np.random.default_rng(4)
+    pool, Hkv, D, T = 30, 4, 64, 40
+    kc = host_values((pool, Hkv, 16, D), "bf16", 1.0, rng)
+    vc = host_values((pool, Hkv, 16, D), "bf16", 1.0, rng)
+    key = host_values((T, Hkv, D), "bf16", 1.0, rng)
+    val = host_values((T, Hkv, D), "bf16", 1.0, rng)
+    slots = rng.permutation(pool * 16)[:T].astype(np.int32)
+    slots[3] = -1
+    ek, ev = kc.copy(), vc.copy()
+    ok = slots >= 0
+    ek[slots[ok] // 16, :, slots[ok] % 16] = key[ok]
+    ev[slots[ok] // 16, :, slots[ok] % 16] = val[ok]
+    oracle_mod.reshape_and_cache(key, val, kc, vc, slots)
+    assert np.array_equal(kc, ek) and np.array_equal(vc, ev)
+
+    ids = rng.permutation(pool)
+    pairs = np.stack([ids[:6], ids[6:12]], 1)
+    ek[pairs[:, 1]] = ek[pairs[:, 0]]
+    ev[pairs[:, 1]] = ev[pairs[:, 0]]
+    oracle_mod.copy_blocks(kc, vc, pairs)
+    assert np.array_equal(kc, ek) and np.array_equal(vc, ev)
+
+    other = np.zeros_like(kc)
+    oracle_mod.swap_blocks(kc, other, pairs)
+    want = np.zeros_like(kc)
+    want[pairs[:, 1]] = kc[pairs[:, 0]]
+    assert np.array_equal(other, want)
+
+    src, dst = np.array([20, 21, 5], np.int32), np.array([2, 3, 5], np.int32)
+    ek[dst], ev[dst] = ek[src], ev[src]
+    oracle_mod.compact_kv_cache(kc, vc, src, dst)
+    assert np.array_equal(kc, ek) and np.array_equal(vc, ev)
+
+    oracle_mod.memset_blocks(kc, np.array([0, 29], np.int32))
+    ek[[0, 29]] = 0
+    assert np.array_equal(kc, ek)
+
+
+def test_compact_oracle_is_parallel_assignment(oracle_mod):
+    """A swap cycle (which races in the concurrent reference kernel) is defined
+    as: every destination receives its source's contents from before the call."""
+    c = np.arange(4 * 16 * 2, dtype=np.float32).reshape(4, 1, 16, 2)
+    v = c.copy()
+    before = c.copy()
+    oracle_mod.compact_kv_cache(c, v, np.array([0, 1], np.int32), np.array([1, 0], np.int32))
+    assert np.array_equal(c[0], before[1]) and np.array_equal(c[1], before[0])
+
+
+@pytest.mark.parametrize("name", list(workloads.WORKLOADS))
+def test_workload_generators_are_consistent(name):
+    w = workloads.make(name)
+    w2 = workloads.make(name)
+    assert np.array_equal(w.context_lens, w2.context_lens) and np.array_equal(w.block_tables, w2.block_tables)
+    nblk = (w.context_lens.astype(np.int64) + 15) // 16
+    assert nblk.max() <= w.block_tables.shape[1]
+    for s in range(w.num_seqs):
+        row = w.block_tables[s, : nblk[s]]
+        assert row.min() >= 0 and row.max() < w.num_blocks
+    # every new token has its own slot, inside the pool, inside its row's blocks
+    assert len(np.unique(w.slot_mapping)) == len(w.slot_mapping)
+    assert w.slot_mapping.min() >= 0 and w.slot_mapping.max() < w.num_blocks * 16
+    for slot, r in zip(w.slot_mapping[:50], w.slot_rows[:50]):
+        pos = w.context_lens[r] - 1
+        assert slot == w.block_tables[r, pos // 16] * 16 + pos % 16
+
+
+def test_workload_sizes_match_the_configs():
+    assert workloads.make("cpu_decode_fp32").num_blocks == 512
+    w = workloads.make("llama2_7b_ragged_decode")
+    assert w.num_seqs == 64 and 1.9e9 < w.kv_bytes() < 2.5e9
+    w = workloads.make("llama3_8b_long_decode")
+    assert w.num_seqs == 16 and w.context_lens.min() >= 16384 and w.context_lens.max() <= 131072
+    w = workloads.make("continuous_batching_mixed")
+    assert w.num_seqs == 224 + 32 * 512 and len(w.slot_mapping) == 16608 and len(w.copy_pairs) == 16
+    assert w.unique_kv_bytes() < w.kv_bytes()
+
+
+GOLDEN_FILES = sorted(GOLDEN.glob("*.npz"))
+
+
+@pytest.mark.skipif(not GOLDEN_FILES, reason="no golden vectors recorded")
+@pytest.mark.parametrize("path", GOLDEN_FILES, ids=lambda p: p.stem)
+def test_oracle_reproduces_golden_vectors(oracle_mod, path):
+    """Golden outputs were produced by CacheFlow's own CUDA kernels
+    (tests/golden/make_golden.py); the oracle must reproduce them."""
+    g = dict(np.load(path))
+    op = str(g["op"])
+    if op == "paged_attention_v1":
+        out = oracle_mod.paged_attention(g["q"], g["k"], g["v"], g["block_tables"], g["context_lens"],
+                                         float(g["scale"]), 0)
+        np.testing.assert_allclose(out, g["out"], rtol=1e-5, atol=1e-5)
+    elif op == "reshape_and_cache":
+        kc, vc = g["k_cache"].copy(), g["v_cache"].copy()
+        oracle_mod.reshape_and_cache(g["key"], g["value"], kc, vc, g["slot_mapping"])
+        assert np.array_equal(kc, g["k_out"]) and np.array_equal(vc, g["v_out"])
+    elif op == "copy_blocks":
+        kc, vc = g["k_cache"].copy(), g["v_cache"].copy()
+        oracle_mod.copy_blocks(kc, vc, g["block_mapping"])
+        assert np.array_equal(kc, g["k_out"]) and np.array_equal(vc, g["v_out"])
+    elif op == "swap_blocks":
+        dst = g["dst"].copy()
+        oracle_mod.swap_blocks(g["src"], dst, g["block_mapping"])
+        assert np.array_equal(dst, g["dst_out"])
+    elif op == "compact_kv_cache":
+        kc, vc = g["k_cache"].copy(), g["v_cache"].copy()
+        oracle_mod.compact_kv_cache(kc, vc, g["src_ids"], g["dst_ids"])
+        assert np.array_equal(kc, g["k_out"]) and np.array_equal(vc, g["v_out"])
+    elif op == "memset_blocks":
+        c = g["cache"].copy()
+        oracle_mod.memset_blocks(c, g["block_ids"])
+        assert np.array_equal(c, g["out"])
+    else:
+        pytest.fail(f"unknown golden op {op}")
