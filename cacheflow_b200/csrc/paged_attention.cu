@@ -33,7 +33,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "cf_device.cuh"
 #include "cf_internal.h"
@@ -122,8 +124,10 @@ struct FmaConsumer {
 
   // One 16-token block; `ntok` valid tokens (1..16).  `pbuf` is this warp's
   // HG*16-float scratch.
-  __device__ __forceinline__ void block(const T* kt, const T* vt, int ntok, float* pbuf,
-                                        int lane) {
+  __device__ __forceinline__ void block(const uint8_t* kraw, const uint8_t* vraw, int ntok,
+                                        float* pbuf, int lane) {
+    const T* kt = reinterpret_cast<const T*>(kraw);
+    const T* vt = reinterpret_cast<const T*>(vraw);
     const int j = lane >> 3;
     const int i = lane & 7;
     float s[4][HG];
@@ -203,6 +207,154 @@ struct FmaConsumer {
 };
 
 // ---------------------------------------------------------------------------
+// Tensor-core consumer for GQA groups (16-bit caches, up to 8 query heads per
+// KV head).  Per 16-token block and warp:
+//   S[16 x 16] = Q[16 x D] . K^T   rows 0..7 = the group's query heads (rows
+//                                  8..15 of Q are zero), 2 n-tiles of 8 tokens
+//   O[16 x D] += P[16 x 16] . V    rows 0..7 carry P rounded to 16 bits, rows
+//                                  8..15 the rounding remainder of the same P,
+//                                  so O = O[g] + O[g+8] keeps ~16 more bits of
+//                                  the softmax weights at no extra MMA cost.
+// K and V tiles arrive through 2-D TMA boxes of 16 rows x 128 bytes with the
+// 128-byte swizzle (16-byte chunk c of row r stored at chunk c ^ (r % 8)), so
+// every ldmatrix phase hits 8 distinct bank groups.  The C fragment of the two
+// S n-tiles is exactly the A fragment of P, so P never leaves registers.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+struct MmaConsumer {
+  static constexpr int kKC = D / 16;  // k-chunks of QK
+  static constexpr int kND = D / 8;   // n-tiles of PV (8 columns each)
+  static constexpr int kBoxBytes = kBlockTokens * 128;
+
+  uint32_t qa[kKC][2];  // A fragment of Q: (row g, k lo) and (row g, k hi)
+  float o[kND][4];      // C fragments of O: rows g (16-bit P) and g+8 (remainder)
+  float m;              // running max of head g (log2 units), uniform in a quad
+  float l;              // this lane's share of the running exp-sum of head g
+  float scale_log2;
+
+  __device__ __forceinline__ void init(const T* qrow, int nheads, float sl2, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int kc = 0; kc < kKC; ++kc) {
+      if (g < nheads) {
+        const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qrow + (size_t)g * D + kc * 16 + 2 * t);
+        qa[kc][0] = q32[0];
+        qa[kc][1] = q32[4];  // +8 elements
+      } else {
+        qa[kc][0] = qa[kc][1] = 0u;
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < kND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    m = -INFINITY;
+    l = 0.f;
+    scale_log2 = sl2;
+  }
+
+  __device__ __forceinline__ void block(const uint8_t* kt, const uint8_t* vt, int ntok, float*,
+                                        int lane) {
+    const int t = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
+    const uint32_t kbase = smem_addr(kt), vbase = smem_addr(vt);
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      // ldmatrix.x4 lane address: matrix mi = (token half, chunk parity).
+      const int r = (mi >> 1) * 8 + ri;
+      const uint32_t rowa = kbase + r * 128;
+#pragma unroll
+      for (int kc = 0; kc < kKC; ++kc) {
+        const int box = kc >> 2;
+        const int c = ((kc & 3) << 1) + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(rowa + box * kBoxBytes + ((c ^ (r & 7)) << 4), b0, b1, b2, b3);
+        mma_16816<T>(s[0], qa[kc][0], 0u, qa[kc][1], 0u, b0, b1);
+        mma_16816<T>(s[1], qa[kc][0], 0u, qa[kc][1], 0u, b2, b3);
+      }
+    }
+    // Online softmax over this block's 16 tokens (4 per lane).
+    float bm = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int tok = nt * 8 + 2 * t + j;
+        const float x = s[nt][j] * scale_log2;
+        s[nt][j] = tok < ntok ? x : -INFINITY;
+        bm = fmaxf(bm, s[nt][j]);
+      }
+    bm = fmaxf(bm, shfl_xor(bm, 1));
+    bm = fmaxf(bm, shfl_xor(bm, 2));
+    const float mn = fmaxf(m, bm);
+    const float mu = (mn == -INFINITY) ? 0.f : mn;
+    const float alpha = exp2f(m - mu);
+    m = mn;
+    float ps = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        s[nt][j] = exp2f(s[nt][j] - mu);
+        ps += s[nt][j];
+      }
+    l = l * alpha + ps;
+#pragma unroll
+    for (int n = 0; n < kND; ++n) {
+      o[n][0] *= alpha;
+      o[n][1] *= alpha;
+      o[n][2] *= alpha;
+      o[n][3] *= alpha;
+    }
+    uint32_t pa[4];
+    split2<T>(s[0][0], s[0][1], pa[0], pa[1]);
+    split2<T>(s[1][0], s[1][1], pa[2], pa[3]);
+
+    if (ntok < kBlockTokens) {
+      // Rows past the context hold whatever the pool holds (possibly NaN);
+      // their weight is 0, but 0 * NaN is not, so clear them before PV.
+      constexpr int kChunksPerRow = D * (int)sizeof(T) / 16;
+      const int n = (kBlockTokens - ntok) * kChunksPerRow;
+      for (int i = lane; i < n; i += 32) {
+        const int r = ntok + i / kChunksPerRow;
+        const int c = i % kChunksPerRow;  // position inside the row is irrelevant
+        *reinterpret_cast<uint4*>(const_cast<uint8_t*>(vt) + (c >> 3) * kBoxBytes + r * 128 +
+                                  ((c & 7) << 4)) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();  // the next TMA write of this tile follows these stores
+      __syncwarp();
+    }
+    {
+      // ldmatrix.x4.trans: matrix mi = (token half, chunk of the pair).
+      const int r = (mi & 1) * 8 + ri;
+      const uint32_t rowa = vbase + r * 128;
+#pragma unroll
+      for (int cp = 0; cp < kND / 2; ++cp) {
+        const int c = 2 * cp + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), b0, b1, b2, b3);
+        mma_16816<T>(o[2 * cp], pa[0], pa[1], pa[2], pa[3], b0, b1);
+        mma_16816<T>(o[2 * cp + 1], pa[0], pa[1], pa[2], pa[3], b2, b3);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void store(float* mo, float* mm, float* ml, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int n = 0; n < kND; ++n) {
+      mo[g * D + n * 8 + 2 * t] = o[n][0] + o[n][2];
+      mo[g * D + n * 8 + 2 * t + 1] = o[n][1] + o[n][3];
+    }
+    float lt = l;
+    lt += shfl_xor(lt, 1);
+    lt += shfl_xor(lt, 2);
+    if (t == 0) {
+      mm[g] = m;
+      ml[g] = lt;
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
 // Kernel configuration (per element type / head dim).
 // ---------------------------------------------------------------------------
 template <typename T, int D, int HG>
@@ -222,10 +374,13 @@ struct AttnConfig {
   static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
 };
 
-template <typename T, int D, int HG>
+template <typename T, int D, int HG, bool kMma>
 __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
-    paged_attention_kernel(const AttnArgs a) {
+    paged_attention_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv) {
   using Cfg = AttnConfig<T, D, HG>;
+  using Consumer = std::conditional_t<kMma, MmaConsumer<T, D>, FmaConsumer<T, D, HG>>;
+  static_assert(!kMma || HG == 8, "the tensor-core consumer covers 8 query heads");
   constexpr int NW = Cfg::kWarps;
   constexpr int S = Cfg::kStages;
   constexpr int TILE = Cfg::kTileBytes;
@@ -269,7 +424,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
   }
   __syncwarp();
 
-  FmaConsumer<T, D, HG> cons;
+  Consumer cons;
   const T* qrow = reinterpret_cast<const T*>(a.q) + ((size_t)seq * a.num_heads + head0) * D;
   cons.init(qrow, nheads, a.scale_log2, lane);
 
@@ -296,10 +451,21 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     flags[s] = 1;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(bar, 2 * TILE);
-    const size_t off = ((size_t)phys * a.num_kv_heads + kvh) * (size_t)TILE;
     uint8_t* kt = tiles + (size_t)s * 2 * TILE;
-    bulk_load(smem_addr(kt), kbase + off, TILE, bar);
-    bulk_load(smem_addr(kt + TILE), vbase + off, TILE, bar);
+    if constexpr (kMma) {
+      // Boxes of 16 rows x 64 elements (128 bytes, swizzled); x stays a
+      // multiple of 64 elements.
+      const int32_t row = (int32_t)(((int64_t)phys * a.num_kv_heads + kvh) * kBlockTokens);
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) {
+        tma_load_2d(smem_addr(kt + b * kBlockTokens * 128), &tmk, b * 64, row, bar);
+        tma_load_2d(smem_addr(kt + TILE + b * kBlockTokens * 128), &tmv, b * 64, row, bar);
+      }
+    } else {
+      const size_t off = ((size_t)phys * a.num_kv_heads + kvh) * (size_t)TILE;
+      bulk_load(smem_addr(kt), kbase + off, TILE, bar);
+      bulk_load(smem_addr(kt + TILE), vbase + off, TILE, bar);
+    }
   };
 
   int ids = fetch_ids(0);
@@ -330,8 +496,8 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     const int blk = pb0 + warp + i * NW;
     const int ntok = min(kBlockTokens, ctx - blk * kBlockTokens);
     if (flags[s]) {
-      const T* kt = reinterpret_cast<const T*>(tiles + (size_t)s * 2 * TILE);
-      cons.block(kt, kt + TILE / (int)sizeof(T), ntok, pbuf, lane);
+      const uint8_t* kt = tiles + (size_t)s * 2 * TILE;
+      cons.block(kt, kt + TILE, ntok, pbuf, lane);
     }
     __syncwarp();
     const int jn = i + S;
@@ -458,11 +624,49 @@ __global__ void __launch_bounds__(D) paged_attention_reduce_kernel(const ReduceA
 // ---------------------------------------------------------------------------
 namespace {
 
-template <typename K>
-cf_status ensure_smem(K kern, int bytes) {
-  // Per-device opt-in to more than 48 KB of dynamic shared memory.
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (EncodeTiledFn) nullptr;
+    }
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// K or V cache viewed as a 2-D tensor [rows = num_blocks*Hkv*16, D] of 16-bit
+// elements, loaded in swizzled boxes of 16 rows x 64 elements (128 bytes).
+bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int32_t dtype) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBlockTokens};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dtype == CF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Per kernel instantiation and device: opt in to > 48 KB of dynamic smem.
+template <typename T, int D, int HG, bool kMma>
+cf_status ensure_smem(int bytes) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
+  auto kern = paged_attention_kernel<T, D, HG, kMma>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -474,16 +678,20 @@ cf_status ensure_smem(K kern, int bytes) {
   return cuda_status(errs[dev]);
 }
 
-template <typename T, int D, int HG>
-cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x) {
+struct Maps {
+  CUtensorMap k, v;
+};
+
+template <typename T, int D, int HG, bool kMma>
+cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& maps) {
   using Cfg = AttnConfig<T, D, HG>;
   const cf_paged_attention_params& p = *l.p;
   a.head_chunks = (a.group + HG - 1) / HG;
-  auto kern = paged_attention_kernel<T, D, HG>;
-  cf_status st = ensure_smem(kern, Cfg::kSmemAlloc);
+  cf_status st = ensure_smem<T, D, HG, kMma>(Cfg::kSmemAlloc);
   if (st != CF_OK) return st;
   dim3 grid((unsigned)grid_x, (unsigned)(p.num_kv_heads * a.head_chunks), (unsigned)p.num_seqs);
-  kern<<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a);
+  paged_attention_kernel<T, D, HG, kMma>
+      <<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a, maps.k, maps.v);
   st = check_launch();
   if (st != CF_OK || l.part_max == nullptr || grid_x == 1) return st;
 
@@ -514,11 +722,31 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x) {
   return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_reduce_kernel<T, D>, r));
 }
 
+// Which consumer runs: tensor cores for GQA groups of 3+ query heads on 16-bit
+// caches, FMA otherwise.  CF_ATTN_CONSUMER=fma|mma overrides (read per call).
+bool use_mma(const cf_paged_attention_params& p, int64_t rows) {
+  if (p.dtype == CF_F32 || p.num_blocks <= 0 || rows > INT32_MAX || p.head_dim % 64 != 0) return false;
+  if (const char* e = std::getenv("CF_ATTN_CONSUMER")) {
+    if (std::strcmp(e, "fma") == 0) return false;
+    if (std::strcmp(e, "mma") == 0) return true;
+  }
+  return p.num_heads / p.num_kv_heads >= 3;
+}
+
 template <typename T, int D>
 cf_status launch_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
-  if (a.group == 1) return launch_typed<T, D, 1>(l, a, grid_x);
-  if (a.group == 2) return launch_typed<T, D, 2>(l, a, grid_x);
-  return launch_typed<T, D, 4>(l, a, grid_x);
+  const cf_paged_attention_params& p = *l.p;
+  Maps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if constexpr (sizeof(T) == 2) {
+    const int64_t rows = p.num_blocks * (int64_t)p.num_kv_heads * kBlockTokens;
+    if (use_mma(p, rows) && kv_tensor_map(&maps.k, p.key_cache, rows, D, p.dtype) &&
+        kv_tensor_map(&maps.v, p.value_cache, rows, D, p.dtype))
+      return launch_typed<T, D, 8, true>(l, a, grid_x, maps);
+  }
+  if (a.group == 1) return launch_typed<T, D, 1, false>(l, a, grid_x, maps);
+  if (a.group == 2) return launch_typed<T, D, 2, false>(l, a, grid_x, maps);
+  return launch_typed<T, D, 4, false>(l, a, grid_x, maps);
 }
 
 template <typename T>

@@ -62,25 +62,25 @@ def main(out_dir: str) -> None:
     kc, vc = f32((pool, Hkv, 16, D)), f32((pool, Hkv, 16, D))
     T = 40
     key, val = f32((T, Hkv, D)), f32((T, Hkv, D))
-    slots = rng.permutation(pool * 16)[:T].astype(np.int32)
-    slots[:2] = [0, pool * 16 - 1]
-    a, b = d(kc), d(vc)
-    assert L.ref_reshape_and_cache(d(key).data_ptr(), d(val).data_ptr(), a.data_ptr(), b.data_ptr(),
-                                   d(slots).data_ptr(), T, Hkv, D, 16) == 0
+    slots = np.concatenate([[0, pool * 16 - 1], 1 + rng.permutation(pool * 16 - 2)[: T - 2]]).astype(np.int32)
+    # every device tensor stays referenced until the kernel has finished
+    a, b, dkey, dval, dslots = d(kc), d(vc), d(key), d(val), d(slots)
+    assert L.ref_reshape_and_cache(dkey.data_ptr(), dval.data_ptr(), a.data_ptr(), b.data_ptr(),
+                                   dslots.data_ptr(), T, Hkv, D, 16) == 0
     np.savez_compressed(out / "reshape_and_cache.npz", op="reshape_and_cache", key=key, value=val, k_cache=kc,
                         v_cache=vc, slot_mapping=slots, k_out=a.cpu().numpy(), v_out=b.cpu().numpy())
 
     ids = rng.permutation(pool)
     pairs = np.stack([ids[:6], ids[6:12]], 1).astype(np.int64)
-    a, b = d(kc), d(vc)
-    assert L.ref_copy_blocks(a.data_ptr(), b.data_ptr(), d(pairs).data_ptr(), len(pairs), Hkv, D, 16) == 0
+    a, b, dpairs = d(kc), d(vc), d(pairs)
+    assert L.ref_copy_blocks(a.data_ptr(), b.data_ptr(), dpairs.data_ptr(), len(pairs), Hkv, D, 16) == 0
     np.savez_compressed(out / "copy_blocks.npz", op="copy_blocks", k_cache=kc, v_cache=vc, block_mapping=pairs,
                         k_out=a.cpu().numpy(), v_out=b.cpu().numpy())
 
     dst = f32((10, Hkv, 16, D))
     sp = np.stack([ids[:5], np.array([9, 0, 4, 2, 7])], 1).astype(np.int64)
-    a, b = d(kc), d(dst)
-    assert L.ref_swap_blocks(a.data_ptr(), b.data_ptr(), d(sp).data_ptr(), len(sp), Hkv * 16 * D * 4) == 0
+    a, b, dsp = d(kc), d(dst), d(sp)
+    assert L.ref_swap_blocks(a.data_ptr(), b.data_ptr(), dsp.data_ptr(), len(sp), Hkv * 16 * D * 4) == 0
     np.savez_compressed(out / "swap_blocks.npz", op="swap_blocks", src=kc, dst=dst, block_mapping=sp,
                         dst_out=b.cpu().numpy())
 
@@ -89,15 +89,15 @@ def main(out_dir: str) -> None:
     holes = [i for i in range(live) if not used[i]]
     movers = [i for i in range(live, pool) if used[i]]
     src, dstids = np.array(movers, np.int32), np.array(holes[: len(movers)], np.int32)
-    a, b = d(kc), d(vc)
-    assert L.ref_compact_kv_cache(a.data_ptr(), b.data_ptr(), d(src).data_ptr(), d(dstids).data_ptr(), len(src),
+    a, b, dsrc, ddst = d(kc), d(vc), d(src), d(dstids)
+    assert L.ref_compact_kv_cache(a.data_ptr(), b.data_ptr(), dsrc.data_ptr(), ddst.data_ptr(), len(src),
                                   Hkv, D, 16) == 0
     np.savez_compressed(out / "compact_kv_cache.npz", op="compact_kv_cache", k_cache=kc, v_cache=vc, src_ids=src,
                         dst_ids=dstids, k_out=a.cpu().numpy(), v_out=b.cpu().numpy())
 
     bids = np.array([0, 5, pool - 1], np.int32)
-    a = d(kc)
-    assert L.ref_memset_blocks(a.data_ptr(), d(bids).data_ptr(), len(bids), Hkv * 16 * D * 4) == 0
+    a, dbids = d(kc), d(bids)
+    assert L.ref_memset_blocks(a.data_ptr(), dbids.data_ptr(), len(bids), Hkv * 16 * D * 4) == 0
     np.savez_compressed(out / "memset_blocks.npz", op="memset_blocks", cache=kc, block_ids=bids,
                         out=a.cpu().numpy())
     print("golden vectors written to", out)

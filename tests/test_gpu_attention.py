@@ -48,9 +48,25 @@ def _oracle(oracle_mod, host, dtype, scale):
     return oracle_mod.paged_attention(q, k, v, tables, ctx, scale, dtype_code=CODE[dtype], num_threads=4)
 
 
+CONSUMERS = ["auto", "fma", "mma"]
+
+
+def _consumer(monkeypatch, dtype, consumer):
+    """Selects the attention consumer (FMA or tensor-core MMA) for 16-bit caches."""
+    if consumer != "auto" and dtype == "f32":
+        pytest.skip("fp32 caches always use the FMA consumer")
+    if consumer == "auto":
+        monkeypatch.delenv("CF_ATTN_CONSUMER", raising=False)
+    else:
+        monkeypatch.setenv("CF_ATTN_CONSUMER", consumer)
+
+
+@pytest.mark.parametrize("consumer", CONSUMERS)
 @pytest.mark.parametrize("dtype,H,Hkv,D,ctx", CASES)
-def test_v1_unsplit_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+def test_v1_unsplit_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, D, ctx, consumer):
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, dtype, consumer)
 
     rng = np.random.default_rng(hash((dtype, H, Hkv, D, len(ctx))) % 2**32)
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
@@ -60,11 +76,14 @@ def test_v1_unsplit_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
     assert ops.device_errors(0) == 0
 
 
+@pytest.mark.parametrize("consumer", CONSUMERS)
 @pytest.mark.parametrize("dtype,H,Hkv,D,ctx", CASES)
-def test_v1_split_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+def test_v1_split_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, D, ctx, consumer):
     import torch
 
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, dtype, consumer)
 
     rng = np.random.default_rng(hash((dtype, H, D, "split")) % 2**32)
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
@@ -76,11 +95,14 @@ def test_v1_split_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
     assert ops.device_errors(0) == 0
 
 
+@pytest.mark.parametrize("consumer", CONSUMERS)
 @pytest.mark.parametrize("dtype,H,Hkv,D,ctx", CASES)
-def test_v2_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+def test_v2_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, D, ctx, consumer):
     import torch
 
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, dtype, consumer)
 
     rng = np.random.default_rng(hash((dtype, H, D, "v2")) % 2**32)
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
@@ -105,12 +127,15 @@ def test_v2_matches_oracle(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
     assert ops.device_errors(0) == 0
 
 
+@pytest.mark.parametrize("consumer", CONSUMERS)
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
-def test_constant_keys_give_mean_of_values(cflib, dtype):
+def test_constant_keys_give_mean_of_values(cflib, monkeypatch, dtype, consumer):
     """Known answer: identical K rows -> uniform softmax -> mean of the V rows."""
     import torch
 
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, dtype, consumer)
 
     rng = np.random.default_rng(7)
     ctx = [1, 16, 37, 600]
@@ -129,7 +154,7 @@ def test_constant_keys_give_mean_of_values(cflib, dtype):
     assert_close(as_f64(d["out"]), want, dtype, "constant K")
 
 
-def test_one_hot_values_recover_weights(cflib, oracle_mod):
+def test_one_hot_values_recover_weights(cflib, oracle_mod, monkeypatch):
     """V[t] = e_{t mod D}: output column d is the total weight of tokens t = d (mod D)."""
     import torch
 
@@ -158,10 +183,13 @@ def test_one_hot_values_recover_weights(cflib, oracle_mod):
         assert abs(got[s, 0].sum() - 1.0) < 1e-5
 
 
-def test_gqa_heads_with_equal_queries_agree(cflib):
+@pytest.mark.parametrize("consumer", CONSUMERS)
+def test_gqa_heads_with_equal_queries_agree(cflib, monkeypatch, consumer):
     import torch
 
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, "bf16", consumer)
 
     rng = np.random.default_rng(3)
     host, d = _setup(rng, "bf16", 8, 2, 128, [77, 1000])
@@ -173,10 +201,13 @@ def test_gqa_heads_with_equal_queries_agree(cflib):
         assert torch.equal(o[:, 4 + h], o[:, 4])
 
 
-def test_empty_context_gives_zeros(cflib):
+@pytest.mark.parametrize("consumer", CONSUMERS)
+def test_empty_context_gives_zeros(cflib, monkeypatch, consumer):
     import torch
 
     from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, "f16", consumer)
 
     rng = np.random.default_rng(5)
     host, d = _setup(rng, "f16", 4, 4, 128, [0, 20, 0])
@@ -186,9 +217,12 @@ def test_empty_context_gives_zeros(cflib):
     assert torch.all(d["out"][1] != 7.0)
 
 
-def test_bad_block_id_is_recorded_not_read(cflib):
+@pytest.mark.parametrize("consumer", CONSUMERS)
+def test_bad_block_id_is_recorded_not_read(cflib, monkeypatch, consumer):
     """An out-of-pool block id is skipped and flagged in the device error word."""
     from cacheflow_b200 import _lib, ops
+
+    _consumer(monkeypatch, "bf16", consumer)
 
     rng = np.random.default_rng(9)
     host, d = _setup(rng, "bf16", 4, 4, 128, [40, 40])
@@ -224,3 +258,26 @@ def test_unsupported_shapes_return_status(cflib):
     with pytest.raises(ops.CacheFlowError) as e:
         ops.paged_attention_v1(torch.empty_like(q), q, k, k, bt, cl, None, 1)
     assert e.value.status == _lib.CF_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("consumer", CONSUMERS)
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_garbage_past_context_does_not_leak(cflib, oracle_mod, monkeypatch, dtype, consumer):
+    """Rows of the last block past the context may hold anything (here NaN)."""
+    import torch
+
+    from cacheflow_b200 import ops
+
+    _consumer(monkeypatch, dtype, consumer)
+    rng = np.random.default_rng(13)
+    ctx = [1, 5, 17, 30, 100]
+    host, d = _setup(rng, dtype, 8, 2, 128, ctx)
+    q, k, v, tables, cl = host
+    for s, c in enumerate(ctx):
+        if c % 16:
+            b = tables[s][c // 16]
+            d["k"][b, :, c % 16:] = float("nan")
+            d["v"][b, :, c % 16:] = float("nan")
+    ops.paged_attention_v1(d["out"], d["q"], d["k"], d["v"], d["bt"], d["cl"], None, max(ctx))
+    want = oracle_mod.paged_attention(q, k, v, tables, cl, 1 / math.sqrt(128), CODE[dtype])
+    assert_close(as_f64(d["out"]), want, dtype, "NaN past context")

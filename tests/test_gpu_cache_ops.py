@@ -33,8 +33,8 @@ def test_reshape_and_cache_bit_exact(cflib, oracle_mod, dtype, Hkv, D):
     pool, T = 64, 200
     kc, vc = _cache(rng, dtype, pool, Hkv, D), _cache(rng, dtype, pool, Hkv, D)
     key, val = host_values((T, Hkv, D), dtype, 1.0, rng), host_values((T, Hkv, D), dtype, 1.0, rng)
-    slots = rng.permutation(pool * 16)[:T].astype(np.int32)
-    slots[[0, 1]] = [0, pool * 16 - 1]  # first and last slot of the pool
+    # distinct slots, including the first and the last slot of the pool
+    slots = np.concatenate([[0, pool * 16 - 1], 1 + rng.permutation(pool * 16 - 2)[: T - 2]]).astype(np.int32)
     slots[5] = -1  # padding token: skipped
     dk, dv = to_dev(kc, dtype), to_dev(vc, dtype)
     ops.reshape_and_cache(to_dev(key, dtype), to_dev(val, dtype), dk, dv, to_dev(slots))
