@@ -141,7 +141,8 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    w = workloads.make(args.workload, seed=1234 + rank)
+    kw = {"num_seqs": args.num_seqs} if args.num_seqs else {}
+    w = workloads.make(args.workload, seed=1234 + rank, **kw)
     tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[w.dtype]
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
@@ -415,6 +416,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama2_7b_ragged_decode", choices=sorted(workloads.WORKLOADS))
     ap.add_argument("--v1-split", choices=["on", "off"], default="on")
+    ap.add_argument("--num-seqs", type=int, default=0,
+                    help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
