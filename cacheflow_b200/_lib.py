@@ -33,6 +33,8 @@ CF_DEVERR_SLOT = 0x2
 CF_DEVERR_CONTEXT_LEN = 0x4
 CF_DEVERR_TIMEOUT = 0x8
 
+CF_STATIC_SCRATCH_BYTES = 16 << 20
+
 
 class AttentionParams(ctypes.Structure):
     """cf_paged_attention_params."""
@@ -65,6 +67,7 @@ SIGNATURES = {
         c_int32,
         [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_int32, c_void_p],
     ),
+    "cf_paged_attention_v2_static_scratch": (c_int32, [POINTER(AttentionParams), c_void_p]),
     "cf_reshape_and_cache": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,

@@ -107,6 +107,32 @@ CF_API cf_status cf_paged_attention_v2(const cf_paged_attention_params* params,
                                 float* tmp_output, int32_t num_partitions,
                                 void* stream);
 
+/* Size of the library's built-in scratch for
+ * cf_paged_attention_v2_static_scratch: 16 MiB, held on every GPU that loads
+ * the library until the process exits. */
+#define CF_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* The same computation as cf_paged_attention_v2 for callers that cannot
+ * allocate device memory: hosts whose own pool already owns all of the GPU's
+ * memory, hosts that must not call cudaMalloc/cudaFree on the decode path
+ * because those calls can synchronise the device, and foreign-function hosts
+ * that hold raw device pointers but no allocator.  The caller passes only the
+ * inputs and the output (params); the partition scratch lives in a fixed
+ * array inside the library, so this call allocates nothing.
+ *
+ * Limit: num_seqs * num_heads * ceil(max_context_len / 512) * (head_dim + 2)
+ * floats (plus alignment) must fit in CF_STATIC_SCRATCH_BYTES; a larger call
+ * returns CF_ERR_WORKSPACE and launches nothing.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture starts.  All calls share the one array, which
+ * keeps the last call's contents (nothing in it needs to start at zero):
+ * calls whose kernels overlap on the GPU -- on different streams, or from
+ * different threads -- race on it and must be serialised by the caller.
+ * This entry point has no counterpart in CacheFlow. */
+CF_API cf_status cf_paged_attention_v2_static_scratch(const cf_paged_attention_params* params,
+                                                      void* stream);
+
 /* Scatter new K/V rows into their cache slots:
  *   cache[slot / block_size, h, slot % block_size, :] = kv[t, h, :]
  * with slot = slot_mapping[t].  A negative slot skips the token (padding).
