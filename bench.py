@@ -219,15 +219,19 @@ def run_ours(args):
         o=torch.empty((S, H, D), dtype=tdt).pin_memory())
     for _ in range(max(3, args.warmup // 4)):
         engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+    engine.synchronize()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    engine.h2d.wait_event(e0)  # the copy streams start inside the timed region too
+    engine.d2h.wait_event(e0)
     e2e_steps = max(1, args.steps // 2)
     for _ in range(e2e_steps):
         engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+    engine.join()  # the last output copy ends the region
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / e2e_steps

@@ -68,7 +68,9 @@ const void* device_view(const void* p) {
   }
 }
 
-cf_status check_attention_params(const cf_paged_attention_params* p) {
+// Shape checks; with check_pointers, also the operands (a size query passes
+// shapes only).
+cf_status check_attention_params(const cf_paged_attention_params* p, bool check_pointers = true) {
   if (p == nullptr) return CF_ERR_INVALID_ARGUMENT;
   if (p->num_seqs < 0 || p->num_heads <= 0 || p->num_kv_heads <= 0) return CF_ERR_INVALID_ARGUMENT;
   if (p->num_heads % p->num_kv_heads != 0) return CF_ERR_INVALID_ARGUMENT;
@@ -78,11 +80,11 @@ cf_status check_attention_params(const cf_paged_attention_params* p) {
   if (p->block_size <= 0 || p->head_dim <= 0) return CF_ERR_INVALID_ARGUMENT;
   if (!cfb::attention_supported(p->head_dim, p->block_size, p->dtype)) return CF_ERR_UNSUPPORTED;
   if (p->num_seqs == 0) return CF_OK;
-  if (p->num_seqs > 65535 || (int64_t)p->num_kv_heads * p->num_heads > 65535)
-    return CF_ERR_UNSUPPORTED;
+  if (p->num_seqs > 65535 || p->num_heads > 65535) return CF_ERR_UNSUPPORTED;  // grid z / y
   if (p->max_blocks_per_seq < 1) return CF_ERR_INVALID_ARGUMENT;
   if ((int64_t)p->max_context_len > (int64_t)p->max_blocks_per_seq * p->block_size)
     return CF_ERR_INVALID_ARGUMENT;
+  if (!check_pointers) return CF_OK;
   if (!p->query || !p->key_cache || !p->value_cache || !p->output || !p->block_tables ||
       !p->context_lens)
     return CF_ERR_INVALID_ARGUMENT;
@@ -127,7 +129,7 @@ const char* cf_status_string(cf_status status) {
 }
 
 size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) {
-  if (check_attention_params(p) != CF_OK) return 0;
+  if (check_attention_params(p, /*check_pointers=*/false) != CF_OK) return 0;
   return v1_split_bytes(p, nullptr);
 }
 

@@ -7,9 +7,15 @@ memory (prepare_kv_cache_inputs, :92-131) and hands those host pointers, a
 null query and a null output to the attention launcher (:137-176).  Here the
 same host-side batch description is staged into device buffers owned by the
 engine, the new K/V rows are scattered into the cache, attention runs on the
-device, and the output is copied back -- all asynchronously on one stream.
-The kernel choice follows the reference: v1 when the longest context is at
-most 8192 tokens, else v2 with 512-token partitions (:162-177).
+device, and the output is copied back.  The kernel choice follows the
+reference: v1 when the longest context is at most 8192 tokens, else v2 with
+512-token partitions (:162-177).
+
+Steps are pipelined over `depth` staging slots and three streams: the
+host-to-device copies of step i+1 and the device-to-host copy of step i-1
+run on the copy engines while step i computes.  Every dependency is an event:
+a slot's inputs are overwritten only after the step that read them finished,
+its output only after it was copied out.
 """
 
 from __future__ import annotations
@@ -21,28 +27,43 @@ from . import ops
 V1_MAX_CONTEXT = 8192  # batch_decode.cpp:163
 
 
+class _Slot:
+    def __init__(self, max_seqs, max_new, num_heads, num_kv_heads, head_dim, max_blocks, dt, dev):
+        self.q = torch.empty((max_seqs, num_heads, head_dim), dtype=dt, device=dev)
+        self.out = torch.empty_like(self.q)
+        self.k_new = torch.empty((max_new, num_kv_heads, head_dim), dtype=dt, device=dev)
+        self.v_new = torch.empty_like(self.k_new)
+        self.slots = torch.empty((max_new,), dtype=torch.int32, device=dev)
+        self.tables = torch.empty((max_seqs, max_blocks), dtype=torch.int32, device=dev)
+        self.ctx = torch.empty((max_seqs,), dtype=torch.int32, device=dev)
+        self.h2d_done = torch.cuda.Event()
+        self.compute_done = torch.cuda.Event()
+        self.d2h_done = torch.cuda.Event()
+        self.used = False
+
+
 class DecodeEngine:
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, num_heads: int,
                  max_seqs: int, max_blocks_per_seq: int, max_new_tokens: int | None = None,
-                 stream: torch.cuda.Stream | None = None, split_v1: bool = True):
+                 stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2):
         self.k = key_cache
         self.v = value_cache
         self.device = key_cache.device
-        num_blocks, self.num_kv_heads, self.block_size, self.head_dim = key_cache.shape
+        _, self.num_kv_heads, self.block_size, self.head_dim = key_cache.shape
         self.num_heads = num_heads
         self.max_seqs = max_seqs
         self.max_blocks_per_seq = max_blocks_per_seq
         self.max_new_tokens = max_new_tokens or max_seqs
         self.stream = stream or torch.cuda.current_stream(self.device)
-        dt = key_cache.dtype
-        dev = self.device
-        self.q = torch.empty((max_seqs, num_heads, self.head_dim), dtype=dt, device=dev)
-        self.out = torch.empty_like(self.q)
-        self.k_new = torch.empty((self.max_new_tokens, self.num_kv_heads, self.head_dim), dtype=dt, device=dev)
-        self.v_new = torch.empty_like(self.k_new)
-        self.slots = torch.empty((self.max_new_tokens,), dtype=torch.int32, device=dev)
-        self.tables = torch.empty((max_seqs, max_blocks_per_seq), dtype=torch.int32, device=dev)
-        self.ctx = torch.empty((max_seqs,), dtype=torch.int32, device=dev)
+        self.h2d = torch.cuda.Stream(self.device)
+        self.d2h = torch.cuda.Stream(self.device)
+        dt, dev = key_cache.dtype, self.device
+        self.slots_ = [_Slot(max_seqs, self.max_new_tokens, num_heads, self.num_kv_heads, self.head_dim,
+                             max_blocks_per_seq, dt, dev) for _ in range(max(1, depth))]
+        self.n = 0
+        # slot 0 doubles as the buffer set of attend() for device-resident inputs
+        s0 = self.slots_[0]
+        self.q, self.out, self.tables, self.ctx = s0.q, s0.out, s0.tables, s0.ctx
         max_ctx = max_blocks_per_seq * self.block_size
         self.workspace = None
         if split_v1:
@@ -65,36 +86,67 @@ class DecodeEngine:
     def d2h_bytes(self, num_seqs: int) -> int:
         return num_seqs * self.num_heads * self.head_dim * self.q.element_size()
 
-    def attend(self, num_seqs: int, max_context_len: int) -> None:
-        """Attention over device-resident inputs (q, tables, ctx already staged)."""
+    def _attend(self, q, out, bt, cl, num_seqs: int, max_context_len: int) -> None:
         S = num_seqs
-        q, out, bt, cl = self.q[:S], self.out[:S], self.tables[:S], self.ctx[:S]
         if max_context_len <= V1_MAX_CONTEXT:
             ops.paged_attention_v1(out, q, self.k, self.v, bt, cl, None, max_context_len, workspace=self.workspace)
-            self.launches_per_step = 1 + (1 if self.workspace is not None and max_context_len > 1024 else 0)
+            split = self.workspace is not None and ops.paged_attention_v1_workspace_size(
+                q, self.k, bt, max_context_len) > 0
+            self.launches_per_step = 2 if split else 1
         else:
-            P = self.parts
             ops.paged_attention_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q, self.k, self.v,
                                    bt, cl, None, max_context_len)
             self.launches_per_step = 2
 
+    def attend(self, num_seqs: int, max_context_len: int) -> None:
+        """Attention over inputs already in self.q / self.tables / self.ctx
+        (the device-resident path), output in self.out; current stream."""
+        S = num_seqs
+        self._attend(self.q[:S], self.out[:S], self.tables[:S], self.ctx[:S], S, max_context_len)
+
     def step(self, q_host, k_new_host, v_new_host, slots_host, tables_host, ctx_host, out_host,
-             max_context_len: int) -> None:
+             max_context_len: int) -> torch.cuda.Event:
         """One decode step from pinned host buffers into pinned `out_host`.
 
         q_host [S, H, D]; k/v_new_host [T, Hkv, D]; slots_host int32 [T];
         tables_host int32 [S, max_blocks_per_seq]; ctx_host int32 [S].
-        Asynchronous on the engine stream; synchronise before reading out_host.
+        Asynchronous: returns the event after which `out_host` holds the
+        result.  The host inputs may be rewritten once the next-but-one step
+        has been submitted (or after synchronize()).
         """
-        S = q_host.shape[0]
-        T = k_new_host.shape[0]
+        S, T = q_host.shape[0], k_new_host.shape[0]
+        b = self.slots_[self.n % len(self.slots_)]
+        self.n += 1
+        if b.used:
+            self.h2d.wait_event(b.compute_done)  # the slot's inputs were read
+        with torch.cuda.stream(self.h2d):
+            b.q[:S].copy_(q_host, non_blocking=True)
+            b.k_new[:T].copy_(k_new_host, non_blocking=True)
+            b.v_new[:T].copy_(v_new_host, non_blocking=True)
+            b.slots[:T].copy_(slots_host, non_blocking=True)
+            b.tables[:S, : tables_host.shape[1]].copy_(tables_host, non_blocking=True)
+            b.ctx[:S].copy_(ctx_host, non_blocking=True)
+            b.h2d_done.record(self.h2d)
+        self.stream.wait_event(b.h2d_done)
+        if b.used:
+            self.stream.wait_event(b.d2h_done)  # the slot's output was copied out
         with torch.cuda.stream(self.stream):
-            self.q[:S].copy_(q_host, non_blocking=True)
-            self.k_new[:T].copy_(k_new_host, non_blocking=True)
-            self.v_new[:T].copy_(v_new_host, non_blocking=True)
-            self.slots[:T].copy_(slots_host, non_blocking=True)
-            self.tables[:S, : tables_host.shape[1]].copy_(tables_host, non_blocking=True)
-            self.ctx[:S].copy_(ctx_host, non_blocking=True)
-            ops.reshape_and_cache(self.k_new[:T], self.v_new[:T], self.k, self.v, self.slots[:T])
-            self.attend(S, max_context_len)
-            out_host.copy_(self.out[:S], non_blocking=True)
+            ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
+            self._attend(b.q[:S], b.out[:S], b.tables[:S], b.ctx[:S], S, max_context_len)
+            b.compute_done.record(self.stream)
+        self.d2h.wait_event(b.compute_done)
+        with torch.cuda.stream(self.d2h):
+            out_host.copy_(b.out[:S], non_blocking=True)
+            b.d2h_done.record(self.d2h)
+        b.used = True
+        return b.d2h_done
+
+    def join(self) -> None:
+        """Makes the compute stream wait for every submitted step's copies."""
+        for b in self.slots_:
+            if b.used:
+                self.stream.wait_event(b.d2h_done)
+
+    def synchronize(self) -> None:
+        for s in (self.h2d, self.stream, self.d2h):
+            s.synchronize()

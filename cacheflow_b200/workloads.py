@@ -240,6 +240,67 @@ def make(name: str, **kw) -> Workload:
 
 
 # ---------------------------------------------------------------------------
+# Device-resident state of a workload (seeded, generated on the GPU).
+# ---------------------------------------------------------------------------
+TORCH_DTYPES = {"f32": "float32", "f16": "float16", "bf16": "bfloat16"}
+
+
+def device_state(w: Workload, device, seed: int = 4321) -> dict:
+    """Caches, query, new K/V rows and index tensors of `w` on `device`."""
+    import torch
+
+    dt = getattr(torch, TORCH_DTYPES[w.dtype])
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    S, H, Hkv, D = w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim
+    T = len(w.slot_mapping)
+    st = {
+        "k_cache": torch.empty(w.cache_shape(), dtype=dt, device=device).normal_(0, w.std, generator=gen),
+        "v_cache": torch.empty(w.cache_shape(), dtype=dt, device=device).normal_(0, w.std, generator=gen),
+        "q": torch.empty((S, H, D), dtype=dt, device=device).normal_(0, w.std, generator=gen),
+        "k_new": torch.empty((T, Hkv, D), dtype=dt, device=device).normal_(0, w.std, generator=gen),
+        "v_new": torch.empty((T, Hkv, D), dtype=dt, device=device).normal_(0, w.std, generator=gen),
+        "slots": torch.from_numpy(w.slot_mapping).to(device),
+        "tables": torch.from_numpy(w.block_tables).to(device),
+        "ctx": torch.from_numpy(w.context_lens).to(device),
+        "pairs": torch.from_numpy(w.copy_pairs).to(device) if len(w.copy_pairs) else None,
+    }
+    return st
+
+
+def gather_rows_for_oracle(w: Workload, st: dict, rows) -> tuple:
+    """Host copies of what rows `rows` of the batch read, with their blocks
+    renumbered into a compact pool: (q, k, v, tables, context_lens) as numpy
+    (bf16 as uint16 bits), small enough for the CPU oracle."""
+    import torch
+
+    rows = np.asarray(rows)
+    ctx = w.context_lens[rows]
+    nblk = (ctx.astype(np.int64) + BLOCK - 1) // BLOCK
+    used = []
+    remap = {}
+    tables = np.zeros((len(rows), int(nblk.max())), np.int32)
+    for i, r in enumerate(rows):
+        for b in range(nblk[i]):
+            old = int(w.block_tables[r, b])
+            if old not in remap:
+                remap[old] = len(used)
+                used.append(old)
+            tables[i, b] = remap[old]
+    idx = torch.tensor(used, dtype=torch.int64, device=st["k_cache"].device)
+    ridx = torch.from_numpy(rows.astype(np.int64)).to(st["q"].device)
+
+    def host(t):
+        t = t.contiguous().cpu()
+        if t.dtype == torch.bfloat16:
+            return t.view(torch.int16).numpy().view(np.uint16)
+        return t.numpy()
+
+    return (host(st["q"].index_select(0, ridx)), host(st["k_cache"].index_select(0, idx)),
+            host(st["v_cache"].index_select(0, idx)), tables, ctx.astype(np.int32))
+
+
+# ---------------------------------------------------------------------------
 # Host-side tensors for parity checks (numpy; bf16 as uint16 bit patterns).
 # ---------------------------------------------------------------------------
 def host_values(shape, dtype: str, std: float, rng: np.random.Generator) -> np.ndarray:

@@ -143,3 +143,18 @@ def test_plan_checker_rejects_races(cflib):
     assert ops.check_compaction_plan(np.array([5, 1]), np.array([1, 2]), 10) == _lib.CF_ERR_PLAN  # chain
     assert ops.check_compaction_plan(np.array([5]), np.array([10]), 10) == _lib.CF_ERR_INVALID_ARGUMENT
     assert ops.check_compaction_plan(np.array([4, 4]), np.array([4, 7]), 10) == _lib.CF_OK  # self move skipped
+
+
+def test_v1_workspace_size_needs_shapes_only(cflib):
+    """The size query is answered from host-side fields; no operand pointers."""
+    from cacheflow_b200 import _lib
+
+    p = _lib.AttentionParams()
+    p.num_seqs, p.num_heads, p.num_kv_heads, p.head_dim, p.block_size = 64, 32, 32, 128, 16
+    p.max_context_len, p.max_blocks_per_seq, p.dtype = 4096, 256, _lib.CF_F16
+    n = cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p))
+    parts = 4096 // 1024
+    rows = 64 * 32 * parts
+    assert n >= rows * (128 + 2) * 4
+    p.max_context_len = 1000  # fits one partition: never splits
+    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == 0

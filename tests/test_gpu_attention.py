@@ -17,7 +17,7 @@ EDGE_CTX = [1, 15, 16, 17, 128, 129, 512, 513]
 CASES = [
     # dtype, num_heads, num_kv_heads, head_dim, context lengths
     ("f32", 4, 4, 128, EDGE_CTX),
-    ("f32", 8, 2, 64, [1, 33, 200, 700]),
+    ("f32", 8, 2, 64, [1, 33, 200, 1700]),
     ("f32", 8, 1, 128, [5, 300]),
     ("f16", 4, 4, 128, EDGE_CTX + [8192, 8193]),
     ("f16", 6, 2, 64, [1, 17, 100, 1500]),
@@ -89,6 +89,7 @@ def test_v1_split_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, 
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
     scale = 1.0 / math.sqrt(D)
     n = ops.paged_attention_v1_workspace_size(d["q"], d["k"], d["bt"], max(ctx))
+    assert (n > 0) == (max(ctx) > 1024)  # contexts past one 1024-token partition split
     ws = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda") if n else None
     ops.paged_attention_v1(d["out"], d["q"], d["k"], d["v"], d["bt"], d["cl"], scale, max(ctx), workspace=ws)
     assert_close(as_f64(d["out"]), _oracle(oracle_mod, host, dtype, scale), dtype, "v1 split")
