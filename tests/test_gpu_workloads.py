@@ -141,7 +141,14 @@ def test_70b_pool_swap_round_trip_and_compaction(cflib):
         assert ops.check_compaction_plan(src, dst, w.num_blocks) == _lib.CF_OK
 
         def checksums(t):
-            return t.view(torch.int16).view(t.shape[0], -1).sum(1, dtype=torch.int64)
+            # per-block sum of the 16-bit patterns, 16K blocks at a time (an
+            # int32 sum of one block cannot overflow: 16,384 values < 2^15)
+            n = t.shape[0]
+            out = torch.empty(n, dtype=torch.int32, device=t.device)
+            flat = t.view(torch.int16).view(n, -1)
+            for i in range(0, n, 16384):
+                out[i:i + 16384] = flat[i:i + 16384].to(torch.int32).sum(1, dtype=torch.int32)
+            return out
 
         ck, cv = checksums(kc), checksums(vc)
         q_rows = np.flatnonzero(keep)
