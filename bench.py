@@ -11,9 +11,12 @@ row once) / step time, in GB/s, summed over ranks; tokens/s (decode rows per
 second per layer) is reported beside it.
 
 Multi-GPU (torchrun, one process per GPU): every rank owns its own block pool
-and batch (weak scaling: the same workload shape per GPU, seeded per rank);
-no collective touches the data path.  Timing is CUDA events on the launching
-stream, max over ranks.
+and no collective touches the data path.  Most workloads scale weakly (every
+rank runs the workload's shape on its own seeded batch); llama3_70b_sharded
+scales strongly (one 1024-sequence batch dealt to the ranks' pools by
+longest-processing-time) and also times its pool operations (4 GB of swap to
+and from pinned host memory, compaction of a half-freed pool).  Timing is CUDA
+events on the launching stream, max over ranks.
 
 --impl reference runs CacheFlow's own CPU decode step (oracle/_ref, built
 from the reference sources) on a bounded sample of the same workload on the
@@ -125,6 +128,87 @@ def fill_normal_(t, std, gen):
     return t.normal_(0.0, std, generator=gen)
 
 
+SHARDED = {"llama3_70b_sharded"}
+
+
+def rank_workload(args, rank: int, world: int):
+    """This rank's batch and the scaling mode.
+
+    Sharded workloads (strong scaling): one global batch, sequences dealt to
+    ranks by longest-processing-time on context length, each rank's share
+    re-homed into its own pool.  The others (weak scaling): every rank runs
+    the workload's full shape on its own seeded batch.
+    """
+    from cacheflow_b200 import sharding
+
+    kw = {"num_seqs": args.num_seqs} if args.num_seqs else {}
+    if args.workload in SHARDED:
+        full = workloads.make(args.workload, seed=1234, **kw)
+        rows = sharding.lpt_assign(full.context_lens, world)[rank]
+        return full.rehome(rows, seed=1234 + rank), "strong"
+    return workloads.make(args.workload, seed=1234 + rank, **kw), "weak"
+
+
+def time_pool_ops(w, k_cache, v_cache, world: int, swap_gb: float):
+    """Timings of the block-movement operators on this rank's pool (the 70B
+    configuration's per-step swap and compaction), CUDA events on the current
+    stream:
+      swap_out / swap_in  swap_gb / world GB of K blocks to / from pinned host
+                          memory with the SM copy kernel (cf_swap_blocks);
+      swap_out_dma        the same through the copy engines (cf_swap_blocks_dma);
+      compact             compaction of the pool after half of its sequences
+                          are freed (cf_compaction_plan + cf_compact_kv_cache).
+    """
+    import torch
+
+    from cacheflow_b200 import ops
+
+    dev = k_cache.device
+    res = {}
+    block_bytes = k_cache[0].numel() * k_cache.element_size()
+    nblk = (w.context_lens.astype(np.int64) + 15) // 16
+    live = np.concatenate([w.block_tables[s, : nblk[s]] for s in range(w.num_seqs)])
+    n = int(min(len(live), (swap_gb / world) * (1 << 30) // block_bytes))
+    rng = np.random.default_rng(7)
+    ids = rng.choice(live, n, replace=False).astype(np.int64)
+    host = torch.empty((n,) + tuple(k_cache.shape[1:]), dtype=k_cache.dtype, pin_memory=True)
+    out_map = torch.from_numpy(np.stack([ids, np.arange(n)], 1)).to(dev)
+    in_map = torch.from_numpy(np.stack([np.arange(n), ids], 1)).to(dev)
+    host_map = np.stack([ids, np.arange(n)], 1)
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / reps
+
+    nbytes = n * block_bytes
+    ms = timed(lambda: ops.swap_blocks(k_cache, host, out_map, stream_tensor=k_cache))
+    res["swap_out"] = {"bytes": nbytes, "ms": round(ms, 3), "GB/s": round(nbytes / ms / 1e6, 1)}
+    ms = timed(lambda: ops.swap_blocks(host, k_cache, in_map, stream_tensor=k_cache))
+    res["swap_in"] = {"bytes": nbytes, "ms": round(ms, 3), "GB/s": round(nbytes / ms / 1e6, 1)}
+    ms = timed(lambda: ops.swap_blocks_dma(k_cache, host, host_map, stream_tensor=k_cache), reps=1)
+    res["swap_out_dma"] = {"bytes": nbytes, "ms": round(ms, 3), "GB/s": round(nbytes / ms / 1e6, 1),
+                           "note": "random block ids: one copy per block"}
+    del host
+    keep = rng.random(w.num_seqs) < 0.5
+    used = np.zeros(w.num_blocks, np.uint8)
+    for s in np.flatnonzero(keep):
+        used[w.block_tables[s, : nblk[s]]] = 1
+    src, dst = ops.compaction_plan(used)
+    s_t, d_t = torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev)
+    moved = 2 * len(src) * 2 * block_bytes  # read + write, K and V
+    ms = timed(lambda: ops.compact_kv_cache(k_cache, v_cache, s_t, d_t), reps=1)
+    res["compact"] = {"moves": int(len(src)), "bytes_read_written": moved, "ms": round(ms, 3),
+                      "GB/s": round(moved / ms / 1e6, 1)}
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -141,8 +225,7 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    kw = {"num_seqs": args.num_seqs} if args.num_seqs else {}
-    w = workloads.make(args.workload, seed=1234 + rank, **kw)
+    w, scaling = rank_workload(args, rank, world)
     tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[w.dtype]
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
@@ -202,8 +285,10 @@ def run_ours(args):
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
-        for _ in range(args.steps):
-            step(record=True)
+        for i in range(args.steps):
+            # the attention launch of every 8th step (and the last) is bracketed
+            # by events for the kernel's own duration; fewer events, less gap
+            step(record=(i % 8 == 0 or i == args.steps - 1))
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
@@ -238,6 +323,18 @@ def run_ours(args):
     if ops.device_errors(local) != 0:
         raise RuntimeError("device error word set during the timed region")
 
+    pool_ops = None
+    if args.workload in SHARDED and not args.no_pool_ops:
+        with torch.cuda.stream(stream):
+            pool_ops = time_pool_ops(w, k_cache, v_cache, world, args.swap_gb)
+        keys = sorted(pool_ops)
+        ms_t = torch.tensor([pool_ops[k]["ms"] for k in keys], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        for k, m in zip(keys, ms_t.tolist()):
+            b = pool_ops[k].get("bytes", pool_ops[k].get("bytes_read_written"))
+            pool_ops[k]["all_ranks_GB/s"] = round(world * b / m / 1e6, 1)
+
     times = torch.tensor([ms_step, att_ms, e2e_ms], dtype=torch.float64, device=dev)
     totals = torch.tensor([w.kv_bytes(), S], dtype=torch.float64, device=dev)
     if world > 1:
@@ -260,7 +357,7 @@ def run_ours(args):
             "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": DTYPE_NAME[w.dtype],
             "data": "synthetic (seeded N(0,%g) caches, shapes of the workload)" % w.std,
@@ -278,7 +375,9 @@ def run_ours(args):
                 "attention": "v1" if mctx <= 8192 else "v2",
                 "v1_split": args.v1_split,
                 "l2": "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (w.kv_bytes() / 1e9),
-                "parallelism": f"dp{world} (sequence-sharded pools, no data-path collective)",
+                "parallelism": (f"dp{world} (one global batch, sequences dealt to per-GPU pools by LPT)"
+                                if scaling == "strong" else
+                                f"dp{world} (per-GPU pools and batches, no data-path collective)"),
             },
             "tokens_per_s": round(seqs_total / (ms_step * 1e-3), 1),
             "frac_of_hbm_peak": round(value / (peak * world), 4),
@@ -305,6 +404,8 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clock_info,
         }
+        if pool_ops is not None:
+            line["pool_ops_rank0"] = pool_ops
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -423,6 +524,8 @@ def main():
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--swap-gb", type=float, default=4.0, help="GB swapped out and in (whole job)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:

@@ -81,6 +81,34 @@ class Workload:
     def cache_shape(self) -> tuple[int, int, int, int]:
         return (self.num_blocks, self.num_kv_heads, BLOCK, self.head_dim)
 
+    def rehome(self, rows, pool_factor: float = 1.2, seed: int = 0) -> "Workload":
+        """Rows `rows` moved into a pool of their own (one GPU's share of a
+        sequence-sharded batch): blocks renumbered into a fresh pool of
+        pool_factor x the blocks they use, ids shuffled; shared blocks stay
+        shared."""
+        rows = np.asarray(rows)
+        rng = np.random.default_rng(seed)
+        ctx = self.context_lens[rows]
+        nblk = (ctx.astype(np.int64) + BLOCK - 1) // BLOCK
+        old_ids = []
+        for i, r in enumerate(rows):
+            old_ids.extend(int(b) for b in self.block_tables[r, : nblk[i]])
+        uniq = list(dict.fromkeys(old_ids))
+        pool = max(1, int(math.ceil(pool_factor * len(uniq))))
+        new = rng.permutation(pool)[: len(uniq)]
+        remap = dict(zip(uniq, new.tolist()))
+        tables = np.zeros((len(rows), max(1, int(nblk.max()) if len(rows) else 1)), np.int32)
+        for i, r in enumerate(rows):
+            tables[i, : nblk[i]] = [remap[int(b)] for b in self.block_tables[r, : nblk[i]]]
+        keep = np.isin(self.slot_rows, rows)
+        pos = {int(r): i for i, r in enumerate(rows)}
+        new_rows = np.array([pos[int(r)] for r in self.slot_rows[keep]], np.int32)
+        slots = np.array([tables[i, (ctx[i] - 1) // BLOCK] * BLOCK + (ctx[i] - 1) % BLOCK for i in new_rows],
+                         np.int32).reshape(-1)
+        w = Workload(self.name, self.num_heads, self.num_kv_heads, self.head_dim, self.dtype, self.std,
+                     ctx.astype(np.int32), tables, pool, slots, new_rows, self.attention, seed=self.seed)
+        return w
+
     def subset(self, rows: np.ndarray) -> "Workload":
         """Same pool, only the given rows (for oracle checks of large batches)."""
         rows = np.asarray(rows)
