@@ -30,18 +30,25 @@ namespace {
 
 constexpr int32_t kV2PartitionTokens = 512;  // CacheFlow's PARTITION_SIZE (paged_attention.cu:368)
 
-// Tokens per partition of the split path of cf_paged_attention_v1; 0 disables
-// splitting.  CF_V1_SPLIT_TOKENS (a multiple of 16) overrides the default.
-int32_t v1_split_tokens() {
-  static int32_t v = [] {
-    int32_t d = 1024;
+// Tokens per partition of the split path of cf_paged_attention_v1: the
+// largest of 1024, 512, 256, 128 that still gives the grid about four CTAs
+// per SM of a B200 (148 SMs) for this batch shape, so small batches spread
+// over the whole GPU while large ones keep long partitions.  0 disables
+// splitting.  CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never) overrides it.
+int32_t v1_split_tokens(const cf_paged_attention_params* p) {
+  static const int32_t forced = [] {
     if (const char* e = std::getenv("CF_V1_SPLIT_TOKENS")) {
       long x = std::strtol(e, nullptr, 10);
-      if (x >= 0 && x % 16 == 0 && x <= (1 << 24)) d = (int32_t)x;
+      if (x >= 0 && x % 16 == 0 && x <= (1 << 24)) return (int32_t)x;
     }
-    return d;
+    return (int32_t)-1;
   }();
-  return v;
+  if (forced >= 0) return forced;
+  constexpr int64_t kTargetCtas = 4 * 148;
+  const int64_t pairs = (int64_t)p->num_seqs * p->num_kv_heads;
+  int32_t split = 1024;
+  while (split > 128 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
+  return split;
 }
 
 // Address under which the current device can dereference `p`, or nullptr if
@@ -95,7 +102,7 @@ cf_status check_attention_params(const cf_paged_attention_params* p, bool check_
 }
 
 size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out) {
-  const int32_t split = v1_split_tokens();
+  const int32_t split = v1_split_tokens(p);
   if (split <= 0 || p->num_seqs <= 0 || p->max_context_len <= split) return 0;
   const int64_t parts = (p->max_context_len + split - 1) / split;
   if (parts_out) *parts_out = (int32_t)parts;
@@ -145,7 +152,7 @@ cf_status cf_paged_attention_v1(const cf_paged_attention_params* p, void* worksp
     const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
     const int64_t r4 = (rows * 4 + 255) / 256 * 256;
     uint8_t* w = static_cast<uint8_t*>(workspace);
-    l.part_tokens = v1_split_tokens();
+    l.part_tokens = v1_split_tokens(p);
     l.num_parts = parts;
     l.part_max = reinterpret_cast<float*>(w);
     l.part_sum = reinterpret_cast<float*>(w + r4);

@@ -584,8 +584,16 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) 
   return r;
 }
 
+constexpr int kReduceThreads = 256;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(D) paged_attention_reduce_kernel(const ReduceArgs r) {
+__global__ void __launch_bounds__(kReduceThreads) paged_attention_reduce_kernel(const ReduceArgs r) {
+  // Threads are (partition group, 4-column slice): each group walks every
+  // kGroups-th partition with float4 loads (a warp reads 512 contiguous bytes
+  // of one partition row), so many partition rows are in flight at once; the
+  // groups' sums are added through shared memory.
+  constexpr int kCols4 = D / 4;
+  constexpr int kGroups = kReduceThreads / kCols4;
   grid_dependency_wait();
   const int h = blockIdx.x;
   const int seq = blockIdx.y;
@@ -599,6 +607,7 @@ __global__ void __launch_bounds__(D) paged_attention_reduce_kernel(const ReduceA
 
   extern __shared__ float wsh[];  // nparts weights
   __shared__ float red[32];
+  __shared__ float4 acc_sh[kGroups][kCols4];
   const size_t base = ((size_t)seq * r.num_heads + h) * r.num_parts;
   float lm = -INFINITY;
   for (int p = threadIdx.x; p < nparts; p += blockDim.x) lm = fmaxf(lm, r.part_max[base + p]);
@@ -610,12 +619,36 @@ __global__ void __launch_bounds__(D) paged_attention_reduce_kernel(const ReduceA
     ls += w;
   }
   const float L = block_reduce(ls, false, red);  // also orders the wsh writes
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
-    const float* po = r.part_out + base * D + d;
-    for (int p = 0; p < nparts; ++p) acc = fmaf(wsh[p], po[(size_t)p * D], acc);
-    reinterpret_cast<T*>(r.out)[((size_t)seq * r.num_heads + h) * D + d] =
-        from_float<T>(L > 0.f ? acc / L : 0.f);
+  const int c4 = threadIdx.x % kCols4;
+  const int grp = threadIdx.x / kCols4;
+  const float4* po = reinterpret_cast<const float4*>(r.part_out + base * D) + c4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int p = grp; p < nparts; p += kGroups) {
+    const float4 v = po[(size_t)p * kCols4];
+    const float w = wsh[p];
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+  }
+  acc_sh[grp][c4] = acc;
+  __syncthreads();
+  if (threadIdx.x < kCols4) {
+    float4 t = acc_sh[0][c4];
+#pragma unroll
+    for (int g = 1; g < kGroups; ++g) {
+      const float4 u = acc_sh[g][c4];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    T* out = reinterpret_cast<T*>(r.out) + ((size_t)seq * r.num_heads + h) * D + c4 * 4;
+    out[0] = from_float<T>(L > 0.f ? t.x / L : 0.f);
+    out[1] = from_float<T>(L > 0.f ? t.y / L : 0.f);
+    out[2] = from_float<T>(L > 0.f ? t.z / L : 0.f);
+    out[3] = from_float<T>(L > 0.f ? t.w / L : 0.f);
   }
 }
 
@@ -711,7 +744,7 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
-  cfg.blockDim = dim3(D);
+  cfg.blockDim = dim3(kReduceThreads);
   cfg.dynamicSmemBytes = rsmem;
   cfg.stream = l.stream;
   cudaLaunchAttribute attr[1];
