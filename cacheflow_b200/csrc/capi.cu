@@ -30,11 +30,11 @@ namespace {
 
 constexpr int32_t kV2PartitionTokens = 512;  // CacheFlow's PARTITION_SIZE (paged_attention.cu:368)
 
-// Tokens per partition of the split path of cf_paged_attention_v1: the
-// largest of 1024, 512, 256, 128 that still gives the grid about four CTAs
-// per SM of a B200 (148 SMs) for this batch shape, so small batches spread
-// over the whole GPU while large ones keep long partitions.  0 disables
-// splitting.  CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never) overrides it.
+// Tokens per partition of the split path of cf_paged_attention_v1: 1024, or
+// 512 when that is needed to give the grid about four CTAs per SM of a B200
+// (148 SMs).  Shorter partitions do not pay: below ~512 tokens the extra
+// reduce launch costs more than the added parallelism.  0 disables splitting;
+// CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never) overrides the choice.
 int32_t v1_split_tokens(const cf_paged_attention_params* p) {
   static const int32_t forced = [] {
     if (const char* e = std::getenv("CF_V1_SPLIT_TOKENS")) {
@@ -47,7 +47,7 @@ int32_t v1_split_tokens(const cf_paged_attention_params* p) {
   constexpr int64_t kTargetCtas = 4 * 148;
   const int64_t pairs = (int64_t)p->num_seqs * p->num_kv_heads;
   int32_t split = 1024;
-  while (split > 128 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
+  while (split > 512 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
   return split;
 }
 

@@ -89,10 +89,10 @@ def test_v1_split_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, 
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
     scale = 1.0 / math.sqrt(D)
     n = ops.paged_attention_v1_workspace_size(d["q"], d["k"], d["bt"], max(ctx))
-    # partitions are 128..1024 tokens: longer contexts always split, shorter never
+    # partitions are 512 or 1024 tokens: longer contexts always split, shorter never
     if max(ctx) > 1024:
         assert n > 0
-    if max(ctx) <= 128:
+    if max(ctx) <= 512:
         assert n == 0
     ws = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda") if n else None
     ops.paged_attention_v1(d["out"], d["q"], d["k"], d["v"], d["bt"], d["cl"], scale, max(ctx), workspace=ws)
