@@ -248,11 +248,27 @@ def run_ours(args):
     pairs = torch.from_numpy(w.copy_pairs).to(dev) if len(w.copy_pairs) else None
     mctx = w.max_context_len
 
-    engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"))
+    chunked = w.has_chunks and args.prefill == "chunked"
+    nc = len(w.chunk_context_lens) if chunked else 0
+    engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
+                          max_chunks=nc)
     engine.q[:S].copy_(q)
     engine.tables.copy_(tables)
     engine.ctx.copy_(ctx)
     stream = engine.stream
+    chunks = None
+    kv_step = w.kv_bytes()
+    if chunked:
+        # decode rows [0, num_decode) through paged attention, the prefill
+        # chunks' tokens through the multi-query operator
+        nd = w.num_decode
+        engine.c_tables[:, : w.chunk_block_tables.shape[1]].copy_(torch.from_numpy(w.chunk_block_tables))
+        engine.c_ctx.copy_(torch.from_numpy(w.chunk_context_lens))
+        engine.c_start.copy_(torch.from_numpy(w.chunk_query_start))
+        max_q = int(np.diff(w.chunk_query_start).max())
+        chunks = (nd, nc, max_q)
+        mctx = int(w.context_lens[:nd].max())
+        kv_step = w.chunked_kv_bytes()
 
     att_ev = []
     # batches that fit in L2 (126 MB) are timed with L2 overwritten between steps
@@ -266,11 +282,11 @@ def run_ours(args):
         if record:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            engine.attend(S, mctx)
+            engine.attend(S, mctx, chunks)
             b.record(stream)
             att_ev.append((a, b))
         else:
-            engine.attend(S, mctx)
+            engine.attend(S, mctx, chunks)
 
     launches_per_step = None
     with torch.cuda.stream(stream):
@@ -319,12 +335,18 @@ def run_ours(args):
     att_ms = sum(a.elapsed_time(b) for a, b in att_ev) / len(att_ev)
 
     # e2e through the public engine API with pinned host buffers.
+    nrows = chunks[0] if chunked else S  # rows described by block tables / context lengths
     pin = dict(
         q=q.cpu().pin_memory(), k=k_new.cpu().pin_memory(), v=v_new.cpu().pin_memory(),
-        s=slots.cpu().pin_memory(), t=tables.cpu().pin_memory(), c=ctx.cpu().pin_memory(),
+        s=slots.cpu().pin_memory(), t=tables[:nrows].cpu().pin_memory(), c=ctx[:nrows].cpu().pin_memory(),
         o=torch.empty((S, H, D), dtype=tdt).pin_memory())
+    chunks_host = None
+    if chunked:
+        chunks_host = (chunks[0], torch.from_numpy(w.chunk_query_start).pin_memory(),
+                       torch.from_numpy(w.chunk_context_lens).pin_memory(),
+                       torch.from_numpy(w.chunk_block_tables).pin_memory())
     for _ in range(max(3, args.warmup // 4)):
-        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
     engine.synchronize()
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -336,7 +358,7 @@ def run_ours(args):
     engine.d2h.wait_event(e0)
     e2e_steps = max(1, args.steps // 2)
     for _ in range(e2e_steps):
-        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx)
+        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
     engine.join()  # the last output copy ends the region
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -357,7 +379,7 @@ def run_ours(args):
             pool_ops[k]["all_ranks_GB/s"] = round(world * b / m / 1e6, 1)
 
     times = torch.tensor([ms_step, att_ms, e2e_ms], dtype=torch.float64, device=dev)
-    totals = torch.tensor([w.kv_bytes(), S], dtype=torch.float64, device=dev)
+    totals = torch.tensor([kv_step, S], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
@@ -366,7 +388,7 @@ def run_ours(args):
 
     if rank == 0:
         peak, peak_kind = hbm_peak()
-        alg_bytes = w.kv_bytes() + w.qo_bytes() + w.table_bytes()
+        alg_bytes = kv_step + w.qo_bytes() + w.table_bytes()
         achieved = alg_bytes / (att_ms * 1e-3) / 1e9
         value = kv_total / (ms_step * 1e-3) / 1e9
         line = {
@@ -392,7 +414,10 @@ def run_ours(args):
                 "context_lens": "min %d / mean %.0f / max %d" % (w.context_lens.min(), w.context_lens.mean(),
                                                                   w.context_lens.max()),
                 "pool_blocks_per_gpu": w.num_blocks,
-                "kv_bytes_per_step_per_gpu": w.kv_bytes(),
+                "kv_bytes_per_step_per_gpu": kv_step,
+                "prefill": ("chunked: %d decode rows + %d chunks through the multi-query operator"
+                            % (chunks[0], chunks[1]) if chunked else
+                            ("one decode row per prefill token" if w.has_chunks else None)),
                 "attention": "v1" if mctx <= 8192 else "v2",
                 "v1_split": args.v1_split,
                 "l2": ("L2 flushed before every timed step (512 MB write, outside the step's events)"
@@ -408,7 +433,8 @@ def run_ours(args):
             "frac_of_hbm_peak": round(value / (peak * world), 4),
             "roofline": {
                 "bound": "hbm",
-                "kernel": "paged_attention" + ("_v1" if mctx <= 8192 else "_v2+reduce"),
+                "kernel": ("paged_attention" + ("_v1" if mctx <= 8192 else "_v2+reduce")
+                           + ("+paged_prefill" if chunked else "")),
                 "achieved": round(achieved, 1),
                 "peak": peak,
                 "unit": "GB/s",
@@ -550,6 +576,8 @@ def main():
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--prefill", choices=["chunked", "rows"], default="chunked",
+                    help="prefill tokens of mixed batches: multi-query chunks or one decode row each")
     ap.add_argument("--swap-gb", type=float, default=4.0, help="GB swapped out and in (whole job)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()

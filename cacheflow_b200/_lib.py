@@ -59,6 +59,30 @@ class AttentionParams(ctypes.Structure):
     ]
 
 
+class PrefillParams(ctypes.Structure):
+    """cf_prefill_params."""
+
+    _fields_ = [
+        ("query", c_void_p),
+        ("key_cache", c_void_p),
+        ("value_cache", c_void_p),
+        ("output", c_void_p),
+        ("block_tables", c_void_p),
+        ("context_lens", c_void_p),
+        ("query_start", c_void_p),
+        ("scale", c_float),
+        ("num_chunks", c_int32),
+        ("num_heads", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("block_size", c_int32),
+        ("max_query_len", c_int32),
+        ("max_blocks_per_seq", c_int32),
+        ("num_blocks", c_int64),
+        ("dtype", c_int32),
+    ]
+
+
 # name -> (restype, argtypes); exactly the functions include/cacheflow_b200.h declares.
 SIGNATURES = {
     "cf_paged_attention_v1": (c_int32, [POINTER(AttentionParams), c_void_p, c_size_t, c_void_p]),
@@ -68,6 +92,7 @@ SIGNATURES = {
         [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_int32, c_void_p],
     ),
     "cf_paged_attention_v2_static_scratch": (c_int32, [POINTER(AttentionParams), c_void_p]),
+    "cf_paged_prefill_attention": (c_int32, [POINTER(PrefillParams), c_void_p]),
     "cf_reshape_and_cache": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,

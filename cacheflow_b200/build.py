@@ -24,7 +24,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libcacheflow_b200.so"
 
-SOURCES = ["paged_attention.cu", "cache_ops.cu", "capi.cu", "static_scratch.cu"]
+SOURCES = ["paged_attention.cu", "prefill_attention.cu", "cache_ops.cu", "capi.cu", "static_scratch.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -175,6 +175,27 @@ cf_status cf_paged_attention_v2(const cf_paged_attention_params* p, float* exp_s
   return launch_paged_attention(l);
 }
 
+cf_status cf_paged_prefill_attention(const cf_prefill_params* p, void* stream) {
+  if (p == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_chunks < 0 || p->num_heads <= 0 || p->num_kv_heads <= 0 ||
+      p->num_heads % p->num_kv_heads != 0 || p->max_query_len < 0 || p->max_blocks_per_seq < 0 ||
+      p->num_blocks < 0 || p->head_dim <= 0 || p->block_size <= 0 || dtype_bytes(p->dtype) == 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (!prefill_supported(p->head_dim, p->block_size, p->dtype, p->num_heads / p->num_kv_heads))
+    return CF_ERR_UNSUPPORTED;
+  if (p->num_chunks == 0 || p->max_query_len == 0) return CF_OK;
+  if (p->num_chunks > 65535 || p->num_kv_heads > 65535) return CF_ERR_UNSUPPORTED;
+  if (p->num_blocks == 0 || p->max_blocks_per_seq < 1) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_blocks * (int64_t)p->num_kv_heads * p->block_size > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  if (!p->query || !p->key_cache || !p->value_cache || !p->output || !p->block_tables ||
+      !p->context_lens || !p->query_start)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->query) || !aligned16(p->key_cache) || !aligned16(p->value_cache) ||
+      !aligned16(p->output))
+    return CF_ERR_INVALID_ARGUMENT;
+  return launch_paged_prefill(*p, (cudaStream_t)stream);
+}
+
 cf_status cf_reshape_and_cache(const void* key, const void* value, void* key_cache,
                                void* value_cache, const int32_t* slot_mapping, int32_t num_tokens,
                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
@@ -325,6 +346,7 @@ cf_status cf_get_device_errors(int32_t device, uint32_t* flags, int32_t clear) {
   st = cuda_status(cudaDeviceSynchronize());
   if (st == CF_OK) st = attention_read_errors(&bits, clear != 0);
   if (st == CF_OK) st = cache_ops_read_errors(&bits, clear != 0);
+  if (st == CF_OK) st = prefill_read_errors(&bits, clear != 0);
   cudaSetDevice(prev);
   *flags = bits;
   return st;

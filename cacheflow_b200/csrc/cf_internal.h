@@ -36,7 +36,15 @@ struct AttnLaunch {
 };
 cf_status launch_paged_attention(const AttnLaunch& l);
 bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype);
+// K or V cache as a 2-D tensor map [rows, D] of 16-bit elements, boxes of
+// 16 rows x 64 elements with the 128-byte swizzle; false if it cannot be encoded.
+bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int32_t dtype);
 cf_status attention_read_errors(uint32_t* bits, bool clear);
+
+// ---- chunked-prefill attention (prefill_attention.cu) ------------------------
+bool prefill_supported(int32_t head_dim, int32_t block_size, int32_t dtype, int32_t group);
+cf_status launch_paged_prefill(const cf_prefill_params& p, cudaStream_t stream);
+cf_status prefill_read_errors(uint32_t* bits, bool clear);
 
 // ---- KV-cache data movement (cache_ops.cu) ---------------------------------
 cf_status launch_reshape_and_cache(const void* key, const void* value, void* key_cache,

@@ -655,8 +655,6 @@ __global__ void __launch_bounds__(kReduceThreads) paged_attention_reduce_kernel(
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-namespace {
-
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // dependency on libcuda).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -664,7 +662,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-EncodeTiledFn encode_tiled() {
+static EncodeTiledFn encode_tiled() {
   static EncodeTiledFn fn = [] {
     void* f = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -693,6 +691,8 @@ bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int3
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+namespace {
 
 // Per kernel instantiation and device: opt in to > 48 KB of dynamic smem.
 template <typename T, int D, int HG, bool kMma>

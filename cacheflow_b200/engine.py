@@ -28,7 +28,7 @@ V1_MAX_CONTEXT = 8192  # batch_decode.cpp:163
 
 
 class _Slot:
-    def __init__(self, max_seqs, max_new, num_heads, num_kv_heads, head_dim, max_blocks, dt, dev):
+    def __init__(self, max_seqs, max_new, num_heads, num_kv_heads, head_dim, max_blocks, dt, dev, max_chunks):
         self.q = torch.empty((max_seqs, num_heads, head_dim), dtype=dt, device=dev)
         self.out = torch.empty_like(self.q)
         self.k_new = torch.empty((max_new, num_kv_heads, head_dim), dtype=dt, device=dev)
@@ -36,6 +36,9 @@ class _Slot:
         self.slots = torch.empty((max_new,), dtype=torch.int32, device=dev)
         self.tables = torch.empty((max_seqs, max_blocks), dtype=torch.int32, device=dev)
         self.ctx = torch.empty((max_seqs,), dtype=torch.int32, device=dev)
+        self.c_tables = torch.empty((max_chunks, max_blocks), dtype=torch.int32, device=dev)
+        self.c_ctx = torch.empty((max_chunks,), dtype=torch.int32, device=dev)
+        self.c_start = torch.empty((max_chunks + 1,), dtype=torch.int32, device=dev)
         self.h2d_done = torch.cuda.Event()
         self.compute_done = torch.cuda.Event()
         self.d2h_done = torch.cuda.Event()
@@ -45,7 +48,8 @@ class _Slot:
 class DecodeEngine:
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, num_heads: int,
                  max_seqs: int, max_blocks_per_seq: int, max_new_tokens: int | None = None,
-                 stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2):
+                 stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2,
+                 max_chunks: int = 0):
         self.k = key_cache
         self.v = value_cache
         self.device = key_cache.device
@@ -59,7 +63,8 @@ class DecodeEngine:
         self.d2h = torch.cuda.Stream(self.device)
         dt, dev = key_cache.dtype, self.device
         self.slots_ = [_Slot(max_seqs, self.max_new_tokens, num_heads, self.num_kv_heads, self.head_dim,
-                             max_blocks_per_seq, dt, dev) for _ in range(max(1, depth))]
+                             max_blocks_per_seq, dt, dev, max_chunks) for _ in range(max(1, depth))]
+        self.c_tables, self.c_ctx, self.c_start = self.slots_[0].c_tables, self.slots_[0].c_ctx, self.slots_[0].c_start
         self.n = 0
         # slot 0 doubles as the buffer set of attend() for device-resident inputs
         s0 = self.slots_[0]
@@ -98,14 +103,29 @@ class DecodeEngine:
                                    bt, cl, None, max_context_len)
             self.launches_per_step = 2
 
-    def attend(self, num_seqs: int, max_context_len: int) -> None:
+    def _attend_mixed(self, b, num_seqs, max_context_len, chunks):
+        """Decode rows [0, num_decode) with paged attention, the remaining rows
+        as prefill chunks with the multi-query operator."""
+        nd, nc, max_q = chunks
+        if nd:
+            self._attend(b.q[:nd], b.out[:nd], b.tables[:nd], b.ctx[:nd], nd, max_context_len)
+        ops.paged_prefill_attention(b.out[nd:num_seqs], b.q[nd:num_seqs], self.k, self.v, b.c_tables[:nc],
+                                    b.c_ctx[:nc], b.c_start[: nc + 1], None, max_q)
+        self.launches_per_step += 1
+
+    def attend(self, num_seqs: int, max_context_len: int, chunks=None) -> None:
         """Attention over inputs already in self.q / self.tables / self.ctx
-        (the device-resident path), output in self.out; current stream."""
+        (the device-resident path), output in self.out; current stream.
+        chunks = (num_decode, num_chunks, max_chunk_len) runs rows past
+        num_decode as prefill chunks (self.c_tables / c_ctx / c_start)."""
         S = num_seqs
+        if chunks is not None:
+            self._attend_mixed(self.slots_[0], S, max_context_len, chunks)
+            return
         self._attend(self.q[:S], self.out[:S], self.tables[:S], self.ctx[:S], S, max_context_len)
 
     def step(self, q_host, k_new_host, v_new_host, slots_host, tables_host, ctx_host, out_host,
-             max_context_len: int) -> torch.cuda.Event:
+             max_context_len: int, chunks_host=None) -> torch.cuda.Event:
         """One decode step from pinned host buffers into pinned `out_host`.
 
         q_host [S, H, D]; k/v_new_host [T, Hkv, D]; slots_host int32 [T];
@@ -113,6 +133,10 @@ class DecodeEngine:
         Asynchronous: returns the event after which `out_host` holds the
         result.  The host inputs may be rewritten once the next-but-one step
         has been submitted (or after synchronize()).
+        chunks_host = (num_decode, query_start int32 [C+1], context_lens int32
+        [C], block_tables int32 [C, max_blocks]): rows past num_decode are the
+        query tokens of C prefill chunks (tables_host / ctx_host then describe
+        the decode rows only).
         """
         S, T = q_host.shape[0], k_new_host.shape[0]
         b = self.slots_[self.n % len(self.slots_)]
@@ -124,15 +148,27 @@ class DecodeEngine:
             b.k_new[:T].copy_(k_new_host, non_blocking=True)
             b.v_new[:T].copy_(v_new_host, non_blocking=True)
             b.slots[:T].copy_(slots_host, non_blocking=True)
-            b.tables[:S, : tables_host.shape[1]].copy_(tables_host, non_blocking=True)
-            b.ctx[:S].copy_(ctx_host, non_blocking=True)
+            nt = tables_host.shape[0]
+            b.tables[:nt, : tables_host.shape[1]].copy_(tables_host, non_blocking=True)
+            b.ctx[:nt].copy_(ctx_host, non_blocking=True)
+            if chunks_host is not None:
+                nd, qs, cc, ct = chunks_host
+                nc = cc.shape[0]
+                b.c_start[: nc + 1].copy_(qs, non_blocking=True)
+                b.c_ctx[:nc].copy_(cc, non_blocking=True)
+                b.c_tables[:nc, : ct.shape[1]].copy_(ct, non_blocking=True)
             b.h2d_done.record(self.h2d)
         self.stream.wait_event(b.h2d_done)
         if b.used:
             self.stream.wait_event(b.d2h_done)  # the slot's output was copied out
         with torch.cuda.stream(self.stream):
             ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
-            self._attend(b.q[:S], b.out[:S], b.tables[:S], b.ctx[:S], S, max_context_len)
+            if chunks_host is not None:
+                nd, qs, cc, _ = chunks_host
+                max_q = int((qs[1:] - qs[:-1]).max()) if cc.shape[0] else 0
+                self._attend_mixed(b, S, max_context_len, (nd, cc.shape[0], max_q))
+            else:
+                self._attend(b.q[:S], b.out[:S], b.tables[:S], b.ctx[:S], S, max_context_len)
             b.compute_done.record(self.stream)
         self.d2h.wait_event(b.compute_done)
         with torch.cuda.stream(self.d2h):

@@ -28,6 +28,7 @@ __all__ = [
     "paged_attention_v1",
     "paged_attention_v1_workspace_size",
     "paged_attention_v2",
+    "paged_prefill_attention",
     "v2_num_partitions",
     "reshape_and_cache",
     "copy_blocks",
@@ -149,6 +150,43 @@ def paged_attention_v2(out, exp_sums, max_logits, tmp_output, query, key_cache, 
     check(lib.cf_paged_attention_v2(ctypes.byref(p), _ptr(exp_sums), _ptr(max_logits),
                                     _ptr(tmp_output), parts, _stream(query)),
           "cf_paged_attention_v2")
+    return out
+
+
+def paged_prefill_attention(out, query, key_cache, value_cache, block_tables, context_lens, query_start,
+                            scale=None, max_query_len=None) -> torch.Tensor:
+    """Chunked-prefill attention (no CacheFlow counterpart).
+
+    query/out: [total query tokens, num_heads, head_dim]; block_tables int32
+    [num_chunks, max_blocks_per_seq]; context_lens int32 [num_chunks] (the
+    chunk's tokens included, already in the cache); query_start int32
+    [num_chunks + 1].  Query token i of chunk c sits at position
+    context_lens[c] - n_c + i and attends causally.
+    """
+    lib = _lib.load()
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_query_len is None:
+        max_query_len = int((query_start[1:] - query_start[:-1]).max().item()) if query_start.numel() > 1 else 0
+    for name, t in (("out", out), ("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
+                    ("block_tables", block_tables), ("context_lens", context_lens), ("query_start", query_start)):
+        if not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, f"{name} must be contiguous")
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    p = _lib.PrefillParams()
+    p.query, p.key_cache, p.value_cache, p.output = _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out)
+    p.block_tables, p.context_lens, p.query_start = _ptr(block_tables), _ptr(context_lens), _ptr(query_start)
+    p.scale = float(scale)
+    p.num_chunks = context_lens.shape[0]
+    p.num_heads = query.shape[1]
+    p.num_kv_heads = num_kv_heads
+    p.head_dim = head_dim
+    p.block_size = block_size
+    p.max_query_len = int(max_query_len)
+    p.max_blocks_per_seq = block_tables.shape[1]
+    p.num_blocks = num_blocks
+    p.dtype = dtype_code(query.dtype)
+    check(lib.cf_paged_prefill_attention(ctypes.byref(p), _stream(query)), "cf_paged_prefill_attention")
     return out
 
 

@@ -47,6 +47,12 @@ class Workload:
     attention: str = "v1"  # "v1" | "v2"
     copy_pairs: np.ndarray = field(default_factory=lambda: np.zeros((0, 2), np.int64))
     seed: int = 0
+    # chunked prefill: rows [num_decode, num_seqs) are the query tokens of the
+    # chunks described below (None when the batch is decode rows only)
+    num_decode: int | None = None
+    chunk_context_lens: np.ndarray | None = None
+    chunk_block_tables: np.ndarray | None = None
+    chunk_query_start: np.ndarray | None = None
 
     @property
     def num_seqs(self) -> int:
@@ -63,6 +69,17 @@ class Workload:
     def kv_bytes(self) -> int:
         """Algorithmic KV bytes one attention pass reads: each (token, kv head) K and V row once."""
         return int(self.context_lens.astype(np.int64).sum()) * 2 * self.num_kv_heads * self.head_dim * self.elem_bytes
+
+    @property
+    def has_chunks(self) -> bool:
+        return self.num_decode is not None
+
+    def chunked_kv_bytes(self) -> int:
+        """KV bytes of one pass with the prefill rows run as chunks: decode rows
+        read their context once, each chunk reads its context once."""
+        row = 2 * self.num_kv_heads * self.head_dim * self.elem_bytes
+        dec = int(self.context_lens[: self.num_decode].astype(np.int64).sum())
+        return (dec + int(self.chunk_context_lens.astype(np.int64).sum())) * row
 
     def unique_kv_bytes(self) -> int:
         """KV bytes of the distinct physical blocks the batch touches (shared prefixes once)."""
@@ -251,6 +268,12 @@ def continuous_batching_mixed(seed: int = 1234) -> Workload:
     w = Workload("continuous_batching_mixed", 32, 8, 128, "bf16", 0.5, ctx, tables, pool,
                  np.array(slots, np.int32), np.array(slot_rows, np.int32), "v1", seed=seed)
     w.copy_pairs = np.stack([np.array(fork_src, np.int64), np.array(fork_dst, np.int64)], 1)
+    # The same prefill work as chunks for the multi-query operator: rows
+    # n_dec.. are the chunks' tokens, chunk-major.
+    w.num_decode = n_dec
+    w.chunk_context_lens = seq_len[n_dec:].astype(np.int32)
+    w.chunk_block_tables = seq_tables[n_dec:].astype(np.int32)
+    w.chunk_query_start = (np.arange(n_pre + 1) * chunk).astype(np.int32)
     return w
 
 

@@ -107,6 +107,41 @@ CF_API cf_status cf_paged_attention_v2(const cf_paged_attention_params* params,
                                 float* tmp_output, int32_t num_partitions,
                                 void* stream);
 
+/* Parameters of one chunked-prefill attention call.  Chunk c owns query
+ * tokens [query_start[c], query_start[c+1]) (its chunk length n_c) and a
+ * sequence whose first context_lens[c] tokens are in the cache, the chunk's
+ * own K/V rows included (write them with cf_reshape_and_cache first).  Query
+ * token i of the chunk sits at position context_lens[c] - n_c + i and attends
+ * to positions 0..that position (causal). */
+typedef struct cf_prefill_params {
+  const void* query;            /* [total query tokens, num_heads, head_dim]  */
+  const void* key_cache;        /* [num_blocks, num_kv_heads, block_size, head_dim] */
+  const void* value_cache;
+  void* output;                 /* [total query tokens, num_heads, head_dim]  */
+  const int32_t* block_tables;  /* [num_chunks, max_blocks_per_seq]          */
+  const int32_t* context_lens;  /* [num_chunks]                               */
+  const int32_t* query_start;   /* [num_chunks + 1], query_start[0] = 0       */
+  float scale;
+  int32_t num_chunks;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;             /* 64 or 128                                  */
+  int32_t block_size;           /* 16                                         */
+  int32_t max_query_len;        /* host-side upper bound of the chunk lengths */
+  int32_t max_blocks_per_seq;
+  int64_t num_blocks;           /* pool size (> 0)                            */
+  int32_t dtype;                /* CF_F16 or CF_BF16                          */
+} cf_prefill_params;
+
+/* Chunked-prefill attention over the paged cache: for every chunk, all its
+ * query tokens x the query heads of one KV head share one stream of the
+ * context through shared memory, on tensor cores.  Equal, within the 16-bit
+ * attention tolerance, to one cf_paged_attention_v1 row per query token with
+ * context length = its position + 1 (what CacheFlow would have to do: it has
+ * no multi-query operator; its forward pass is the abstract ForwardFn of
+ * batch_decode.h:34-42). */
+CF_API cf_status cf_paged_prefill_attention(const cf_prefill_params* params, void* stream);
+
 /* Size of the library's built-in scratch for
  * cf_paged_attention_v2_static_scratch: 16 MiB, held on every GPU that loads
  * the library until the process exits. */

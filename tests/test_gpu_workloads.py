@@ -97,6 +97,18 @@ def test_full_size_workload(cflib, oracle_mod, name):
             lim = 2 * atol + 2 * rtol * out.double().abs()
             assert bool((err <= lim).all()), f"{name}: {mode} vs {main} max err {err.max().item():.3e}"
             del other
+        if w.has_chunks:
+            # the prefill chunks through the multi-query operator agree with
+            # their per-token decode rows
+            nd = w.num_decode
+            pre = torch.empty_like(out[nd:])
+            ops.paged_prefill_attention(pre, st["q"][nd:], st["k_cache"], st["v_cache"],
+                                        torch.from_numpy(w.chunk_block_tables).cuda(),
+                                        torch.from_numpy(w.chunk_context_lens).cuda(),
+                                        torch.from_numpy(w.chunk_query_start).cuda())
+            ref = out[nd:].double()
+            err = (pre.double() - ref).abs()
+            assert bool((err <= 2 * atol + 2 * rtol * ref.abs()).all()), f"chunked prefill max err {err.max().item():.3e}"
         assert ops.device_errors(0) == 0
     finally:
         del st
