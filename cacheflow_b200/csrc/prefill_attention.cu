@@ -20,8 +20,10 @@
 //   * rows past the context or of an out-of-pool block are zeroed in the V
 //     fragments (registers), never read as garbage.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "cf_device.cuh"
 #include "cf_internal.h"
@@ -354,28 +356,402 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
   }
 }
 
+// ---------------------------------------------------------------------------
+// The same operator on 5th-generation tensor cores (tcgen05).  One CTA owns
+// 128 query rows (the M of every MMA) and 6 warps:
+//   warps 0-3  softmax and epilogue: thread = row, tensor-memory lane = row;
+//   warp 4     TMA producer (64-key stages of K and V, 3-stage ring);
+//   warp 5     tensor-memory owner and MMA issuer (one thread).
+// Tensor memory (256 columns): S double-buffered at columns [0,64) and
+// [64,128), the O accumulator at [128, 128 + D).
+// Per stage: S = Q K^T (M 128, N 64, K = D; Q and K as K-major operands in
+// 128-byte-swizzled shared memory), the softmax warps read S, mask, update
+// the running max / sum and write P (16-bit head and remainder, two K-major
+// A operands), then O += P_hi V + P_lo V (V as an MN-major B operand).  O is
+// rescaled (tcgen05.ld / st) only when a row's max grows by more than 2^8:
+// until then P may exceed 1 by at most 2^8, which f32 accumulation absorbs.
+// K and V tiles are placed box-major ([64-column box][4 blocks][16 rows][128 B])
+// so one descriptor spans the 64 keys of a stage with an 8-row stride of
+// 1024 bytes.  Completion: tcgen05.commit -> mbarriers; all waits bounded.
+// ---------------------------------------------------------------------------
 namespace {
 
-template <typename T, int D>
-cf_status launch_prefill_typed(const cf_prefill_params& p, cudaStream_t stream) {
-  using L = PrefillLayout<D>;
-  static std::once_flag flags[64];
-  static cudaError_t errs[64];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e);
-  auto kern = paged_prefill_kernel<T, D>;
-  if (dev < 0 || dev >= 64) return CF_ERR_UNSUPPORTED;
-  std::call_once(flags[dev], [&] {
-    errs[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-  });
-  if (errs[dev] != cudaSuccess) return cuda_status(errs[dev]);
+constexpr int kTcRows = 128;
+constexpr int kTcThreads = 6 * 32;
+constexpr int kTcProducerWarp = 4;
+constexpr int kTcMmaWarp = 5;
+constexpr int kTcStages = 3;
+constexpr int kTcStageKeys = kStageBlocks * kPBlock;  // 64
+constexpr uint32_t kTcTmemCols = 256;
+constexpr uint32_t kTcOCol = 128;
+constexpr float kRescaleLog2 = 8.f;
 
-  const int64_t rows = p.num_blocks * (int64_t)p.num_kv_heads * kPBlock;
-  CUtensorMap tmk, tmv;
-  if (!kv_tensor_map(&tmk, p.key_cache, rows, D, p.dtype) ||
-      !kv_tensor_map(&tmv, p.value_cache, rows, D, p.dtype))
-    return CF_ERR_INVALID_ARGUMENT;
+template <int D>
+struct TcLayout {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kQBox = kTcRows * 128;         // 16 KB: 128 rows x 128 B
+  static constexpr int kQBytes = kBoxes * kQBox;
+  static constexpr int kKVBox = kTcStageKeys * 128;   // 8 KB: 64 keys x 128 B
+  static constexpr int kKBytes = kBoxes * kKVBox;
+  static constexpr int kStage = 2 * kKBytes;          // K, then V
+  static constexpr int kPBytes = kTcRows * 128;       // 128 rows x 64 keys x 2 B
+  static constexpr int kRingOff = kQBytes;
+  static constexpr int kPOff = kRingOff + kTcStages * kStage;  // P head, then remainder
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kNumBars = 2 * kTcStages + 5;  // kv_full, kv_empty, s_full x2, p_full, o_done, fin
+  static constexpr int kMaskOff = kBarOff + kNumBars * 8;
+  static constexpr int kTmemOff = kMaskOff + kTcStages * 4;
+  static constexpr int kBytes = kTmemOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
+}  // namespace
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    paged_prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv) {
+  using L = TcLayout<D>;
+  constexpr uint32_t kAB = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t kIdescQK = tc_idesc_f16(kAB, 0, kTcRows, kTcStageKeys);
+  constexpr uint32_t kIdescPV = tc_idesc_f16(kAB, 1, kTcRows, D);
+  constexpr int kBoxBytes = kPBlock * 128;  // one block's 16 rows of one box
+
+  const int tile = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int chunk = blockIdx.z;
+  const int q0 = a.query_start[chunk];
+  const int qlen = a.query_start[chunk + 1] - q0;
+  const int tok0 = tile * a.tokens_per_tile;
+  if (qlen <= 0 || tok0 >= qlen) return;
+  const int cap = a.max_blocks_per_seq * kPBlock;
+  int ctx = a.context_lens[chunk];
+  if (ctx < qlen || ctx > cap) {
+    if (threadIdx.x == 0 && tile == 0 && kvh == 0) prefill_error(CF_DEVERR_CONTEXT_LEN);
+    if (qlen > cap) return;
+    ctx = ctx < qlen ? qlen : cap;
+  }
+  const int ntok = min(a.tokens_per_tile, qlen - tok0);
+  const int pos0 = ctx - qlen + tok0;
+  const int nblk = (pos0 + ntok - 1) / kPBlock + 1;
+  const int nstages = (nblk + kStageBlocks - 1) / kStageBlocks;
+  const int G = a.group;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + kTcStages;
+  uint64_t* s_full = bars + 2 * kTcStages;  // two
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 1;
+  uint64_t* fin = o_done + 1;
+  int* vmask = reinterpret_cast<int*>(smem + L::kMaskOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemOff);
+  const uint32_t q_base = smem_addr(smem);
+  const uint32_t p_base = smem_addr(smem + L::kPOff);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(smem_addr(&kv_full[s]), 1);
+      mbar_init(smem_addr(&kv_empty[s]), 1);
+    }
+    mbar_init(smem_addr(&s_full[0]), 1);
+    mbar_init(smem_addr(&s_full[1]), 1);
+    mbar_init(smem_addr(p_full), 4 * 32);
+    mbar_init(smem_addr(o_done), 1);
+    mbar_init(smem_addr(fin), 1);
+    fence_mbar_init();
+  }
+  if (warp == kTcMmaWarp) {
+    tmem_alloc(smem_addr(tmem_slot), kTcTmemCols);
+    tmem_relinquish();
+  }
+  // Q tile -> shared memory, K-major with the 128-byte swizzle: row r,
+  // 16-byte chunk c of its D elements at box c/8, line r, chunk (c%8)^(r%8).
+  {
+    constexpr int kChunks = D / 8;
+    for (int i = threadIdx.x; i < kTcRows * kChunks; i += kTcThreads) {
+      const int r = i / kChunks, c = i - (i / kChunks) * kChunks;
+      const int t = r / G, h = r - t * G;
+      const bool act = (t < ntok) && (r < a.tokens_per_tile * G);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (act)
+        v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.q) +
+                                            (((size_t)q0 + tok0 + t) * a.num_heads + (size_t)kvh * G + h) * D +
+                                            c * 8);
+      *reinterpret_cast<uint4*>(smem + (c >> 3) * L::kQBox + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int32_t* table = a.block_tables + (size_t)chunk * a.max_blocks_per_seq;
+
+  if (warp == kTcProducerWarp) {
+    // ---------------- TMA producer ----------------
+    int ids = 0, issued = 0;
+    for (int st = 0; st < nstages; ++st) {
+      const int slot = st % kTcStages;
+      if (st >= kTcStages) {
+        bool ready = true;
+        if (lane == 0)
+          ready = mbar_wait_bounded(smem_addr(&kv_empty[slot]), (uint32_t)((st / kTcStages) - 1) & 1u);
+        if (__shfl_sync(0xffffffffu, ready ? 1 : 0, 0) == 0) {
+          if (lane == 0) prefill_error(CF_DEVERR_TIMEOUT);
+          break;
+        }
+      }
+      const int b0 = st * kStageBlocks;
+      if ((b0 & 31) == 0) ids = (b0 + lane < nblk) ? table[b0 + lane] : 0;
+      int phys[kStageBlocks];
+#pragma unroll
+      for (int k = 0; k < kStageBlocks; ++k) phys[k] = __shfl_sync(0xffffffffu, ids, (b0 + k) & 31);
+      if (lane == 0) {
+        int mask = 0, nvalid = 0;
+#pragma unroll
+        for (int k = 0; k < kStageBlocks; ++k) {
+          if (b0 + k >= nblk) continue;
+          if (phys[k] < 0 || (int64_t)phys[k] >= a.num_blocks) {
+            prefill_error(CF_DEVERR_BLOCK_ID);
+            continue;
+          }
+          mask |= 1 << k;
+          ++nvalid;
+        }
+        vmask[slot] = mask;
+        const uint32_t bar = smem_addr(&kv_full[slot]);
+        uint8_t* stage = smem + L::kRingOff + (size_t)slot * L::kStage;
+        fence_proxy_async_smem();
+        if (nvalid == 0) {
+          mbar_arrive(bar);
+        } else {
+          mbar_arrive_expect_tx(bar, (uint32_t)(nvalid * 2 * kPBlock * D * 2));
+#pragma unroll
+          for (int k = 0; k < kStageBlocks; ++k) {
+            if (!(mask & (1 << k))) continue;
+            const int32_t row = (int32_t)(((int64_t)phys[k] * a.num_kv_heads + kvh) * kPBlock);
+#pragma unroll
+            for (int b = 0; b < L::kBoxes; ++b) {
+              tma_load_2d(smem_addr(stage + b * L::kKVBox + k * kBoxBytes), &tmk, b * 64, row, bar);
+              tma_load_2d(smem_addr(stage + L::kKBytes + b * L::kKVBox + k * kBoxBytes), &tmv, b * 64, row,
+                          bar);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      issued = st + 1;
+    }
+    if (lane == 0) {
+      const int first = issued > kTcStages ? issued - kTcStages : 0;
+      for (int st = first; st < issued; ++st)
+        mbar_wait_bounded(smem_addr(&kv_full[st % kTcStages]), (uint32_t)(st / kTcStages) & 1u);
+    }
+  } else if (warp == kTcMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      bool ok = true;
+      auto issue_qk = [&](int st) {
+        const uint32_t kb = smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage);
+        const uint32_t d = tmem + (uint32_t)((st & 1) * kTcStageKeys);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = smem_desc_sw128(q_base + (kk >> 2) * L::kQBox + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(kb + (kk >> 2) * L::kKVBox + (kk & 3) * 32, 16, 1024);
+          tc_mma_f16(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_addr(&s_full[st & 1]));
+      };
+      if (mbar_wait_bounded(smem_addr(&kv_full[0]), 0)) {
+        tc_fence_after();
+        issue_qk(0);
+      } else {
+        ok = false;
+      }
+      for (int st = 0; ok && st < nstages; ++st) {
+        if (st + 1 < nstages) {
+          if (!mbar_wait_bounded(smem_addr(&kv_full[(st + 1) % kTcStages]),
+                                 (uint32_t)((st + 1) / kTcStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk(st + 1);
+        }
+        if (!mbar_wait_bounded(smem_addr(p_full), (uint32_t)st & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t vb =
+            smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage + L::kKBytes);
+#pragma unroll
+        for (int j = 0; j < kStageBlocks; ++j) {
+#pragma unroll
+          for (int hl = 0; hl < 2; ++hl) {
+            const uint64_t ad = smem_desc_sw128(p_base + hl * L::kPBytes + j * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(vb + j * kBoxBytes, L::kKVBox, 1024);
+            tc_mma_f16(tmem + kTcOCol, ad, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(smem_addr(o_done));
+        tc_commit(smem_addr(&kv_empty[st % kTcStages]));
+      }
+      if (!ok) prefill_error(CF_DEVERR_TIMEOUT);
+      // Every MMA issued above has finished before tensor memory is released.
+      tc_commit(smem_addr(fin));
+      mbar_wait_bounded(smem_addr(fin), 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax warps: thread = row ----------------
+    const int r = 32 * warp + lane;
+    const int t = r / G, h = r - t * G;
+    const bool act = (t < ntok) && (r < a.tokens_per_tile * G);
+    const int qpos = act ? pos0 + t : -1;
+    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int st = 0; st < nstages; ++st) {
+      const int slot = st % kTcStages;
+      const bool r1 = mbar_wait_bounded(smem_addr(&s_full[st & 1]), (uint32_t)(st >> 1) & 1u);
+      const bool r2 = mbar_wait_bounded(smem_addr(&kv_full[slot]), (uint32_t)(st / kTcStages) & 1u);
+      if (!__all_sync(0xffffffffu, r1 && r2)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kTcStageKeys];
+      {
+        float(&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
+        float(&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
+        tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys), s0);
+        tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys + 32), s1);
+        tmem_wait_ld();
+      }
+      const int mask = vmask[slot];
+      const int key0 = st * kTcStageKeys;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kTcStageKeys; ++j) {
+        const bool valid = ((mask >> (j >> 4)) & 1) && (key0 + j <= qpos);
+        s[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[j]);
+      }
+      float alpha = 1.f;
+      if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleLog2)) {
+        alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
+        m_run = mx;
+      }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < kTcStageKeys; ++j) {
+        s[j] = exp2f(s[j] - mu);
+        ps += s[j];
+      }
+      l_run = l_run * alpha + ps;
+      if (st > 0) {
+        // PV of the previous stage reads P and writes O: wait for it.
+        const bool r3 = mbar_wait_bounded(smem_addr(o_done), (uint32_t)(st - 1) & 1u);
+        if (!__all_sync(0xffffffffu, r3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tmem_ld32(trow + kTcOCol + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(trow + kTcOCol + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P (16-bit head and remainder) as two K-major A operands.
+#pragma unroll
+      for (int c = 0; c < kTcStageKeys / 8; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split2<T>(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
+        uint8_t* dst = smem + L::kPOff + r * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(dst + L::kPBytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      // V rows the MMA must not multiply (not loaded this stage, past the
+      // context, or of a rejected block) are cleared: 0 * NaN would not be 0.
+      {
+        const int keys_loaded = min(kTcStageKeys, nblk * kPBlock - key0);
+        const int keys_ctx = min(kTcStageKeys, ctx - key0);
+        const int keep = min(keys_loaded, keys_ctx);
+        const int full_mask = (1 << min(kStageBlocks, nblk - st * kStageBlocks)) - 1;
+        if (keep < kTcStageKeys || mask != full_mask) {
+          uint8_t* vst = smem + L::kRingOff + (size_t)slot * L::kStage + L::kKBytes;
+          for (int i = threadIdx.x; i < kTcStageKeys * L::kBoxes * 8; i += 4 * 32) {
+            const int key = i / (L::kBoxes * 8);
+            const int rem = i - key * (L::kBoxes * 8);
+            const int b = rem >> 3, c = rem & 7;
+            const bool bad = key >= keep || !((mask >> (key >> 4)) & 1);
+            if (bad)
+              *reinterpret_cast<uint4*>(vst + b * L::kKVBox + key * 128 + (c << 4)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_addr(p_full));
+    }
+    if (ok) {
+      const bool r4 = mbar_wait_bounded(smem_addr(o_done), (uint32_t)(nstages - 1) & 1u);
+      if (__all_sync(0xffffffffu, r4)) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* out = reinterpret_cast<T*>(a.out) +
+                 (((size_t)q0 + tok0 + (act ? t : 0)) * a.num_heads + (size_t)kvh * G + h) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(trow + kTcOCol + c * 32, o);
+          tmem_wait_ld();
+          if (act) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = pack2<T>(o[2 * i] * inv, o[2 * i + 1] * inv);
+            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+          }
+        }
+      } else {
+        ok = false;
+      }
+    }
+    if (!ok && lane == 0) prefill_error(CF_DEVERR_TIMEOUT);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTcMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+}
+
+namespace {
+
+PrefillArgs make_args(const cf_prefill_params& p, int rows_per_cta) {
   PrefillArgs a;
   a.q = p.query;
   a.out = p.output;
@@ -387,12 +763,61 @@ cf_status launch_prefill_typed(const cf_prefill_params& p, cudaStream_t stream) 
   a.num_kv_heads = p.num_kv_heads;
   a.group = p.num_heads / p.num_kv_heads;
   a.max_blocks_per_seq = p.max_blocks_per_seq;
-  a.tokens_per_tile = kRows / a.group;
+  a.tokens_per_tile = rows_per_cta / a.group;
   a.num_blocks = p.num_blocks;
+  return a;
+}
+
+// Opts a kernel into its dynamic shared memory once per device.
+template <typename Kernel>
+cf_status ensure_prefill_smem(Kernel kern, int bytes, std::once_flag* flags, cudaError_t* errs) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64) return CF_ERR_UNSUPPORTED;
+  std::call_once(flags[dev], [&] {
+    errs[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  return errs[dev] == cudaSuccess ? CF_OK : cuda_status(errs[dev]);
+}
+
+template <typename T, int D>
+cf_status launch_prefill_typed(const cf_prefill_params& p, bool tcgen05, cudaStream_t stream) {
+  const int64_t rows = p.num_blocks * (int64_t)p.num_kv_heads * kPBlock;
+  CUtensorMap tmk, tmv;
+  if (!kv_tensor_map(&tmk, p.key_cache, rows, D, p.dtype) ||
+      !kv_tensor_map(&tmv, p.value_cache, rows, D, p.dtype))
+    return CF_ERR_INVALID_ARGUMENT;
+  if (tcgen05) {
+    static std::once_flag flags[64];
+    static cudaError_t errs[64];
+    cf_status s = ensure_prefill_smem(paged_prefill_tc_kernel<T, D>, TcLayout<D>::kAlloc, flags, errs);
+    if (s != CF_OK) return s;
+    const PrefillArgs a = make_args(p, kTcRows);
+    const int tiles = (p.max_query_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
+    dim3 grid((unsigned)tiles, (unsigned)p.num_kv_heads, (unsigned)p.num_chunks);
+    paged_prefill_tc_kernel<T, D><<<grid, kTcThreads, TcLayout<D>::kAlloc, stream>>>(a, tmk, tmv);
+    return check_launch();
+  }
+  static std::once_flag flags[64];
+  static cudaError_t errs[64];
+  cf_status s = ensure_prefill_smem(paged_prefill_kernel<T, D>, PrefillLayout<D>::kAlloc, flags, errs);
+  if (s != CF_OK) return s;
+  const PrefillArgs a = make_args(p, kRows);
   const int tiles = (p.max_query_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
   dim3 grid((unsigned)tiles, (unsigned)p.num_kv_heads, (unsigned)p.num_chunks);
-  paged_prefill_kernel<T, D><<<grid, (kConsumerWarps + 1) * 32, L::kAlloc, stream>>>(a, tmk, tmv);
+  paged_prefill_kernel<T, D><<<grid, (kConsumerWarps + 1) * 32, PrefillLayout<D>::kAlloc, stream>>>(a, tmk, tmv);
   return check_launch();
+}
+
+// The tcgen05 kernel by default; CF_PREFILL_CONSUMER=mma selects the
+// mma.sync kernel (=tc the tcgen05 one).
+bool use_tcgen05() {
+  if (const char* e = std::getenv("CF_PREFILL_CONSUMER")) {
+    if (std::strcmp(e, "tc") == 0) return true;
+    if (std::strcmp(e, "mma") == 0) return false;
+  }
+  return true;
 }
 
 }  // namespace
@@ -404,12 +829,13 @@ bool prefill_supported(int32_t head_dim, int32_t block_size, int32_t dtype, int3
 
 cf_status launch_paged_prefill(const cf_prefill_params& p, cudaStream_t stream) {
   if (p.num_chunks == 0 || p.max_query_len == 0) return CF_OK;
+  const bool tc = use_tcgen05();
   if (p.dtype == CF_BF16) {
-    if (p.head_dim == 128) return launch_prefill_typed<__nv_bfloat16, 128>(p, stream);
-    return launch_prefill_typed<__nv_bfloat16, 64>(p, stream);
+    if (p.head_dim == 128) return launch_prefill_typed<__nv_bfloat16, 128>(p, tc, stream);
+    return launch_prefill_typed<__nv_bfloat16, 64>(p, tc, stream);
   }
-  if (p.head_dim == 128) return launch_prefill_typed<__half, 128>(p, stream);
-  return launch_prefill_typed<__half, 64>(p, stream);
+  if (p.head_dim == 128) return launch_prefill_typed<__half, 128>(p, tc, stream);
+  return launch_prefill_typed<__half, 64>(p, tc, stream);
 }
 
 cf_status prefill_read_errors(uint32_t* bits, bool clear) {

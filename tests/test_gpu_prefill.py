@@ -12,6 +12,15 @@ from helpers import CODE, as_f64, assert_close, random_tables, to_dev, torch_dty
 
 pytestmark = pytest.mark.gpu
 
+CONSUMERS = ["mma", "tc"]
+
+
+@pytest.fixture(params=CONSUMERS)
+def consumer(request, monkeypatch):
+    """Selects the prefill kernel: mma.sync warps or tcgen05 with tensor memory."""
+    monkeypatch.setenv("CF_PREFILL_CONSUMER", request.param)
+    return request.param
+
 
 def _case(rng, dtype, H, Hkv, D, chunks):
     """chunks: list of (tokens already cached, chunk length)."""
@@ -58,7 +67,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("dtype,H,Hkv,D,chunks", CASES)
-def test_prefill_matches_oracle_rows(cflib, oracle_mod, dtype, H, Hkv, D, chunks):
+def test_prefill_matches_oracle_rows(cflib, oracle_mod, consumer, dtype, H, Hkv, D, chunks):
     from cacheflow_b200 import ops
 
     rng = np.random.default_rng(hash((dtype, H, Hkv, D, len(chunks))) % 2**32)
@@ -70,7 +79,7 @@ def test_prefill_matches_oracle_rows(cflib, oracle_mod, dtype, H, Hkv, D, chunks
     assert ops.device_errors(0) == 0
 
 
-def test_prefill_agrees_with_decode_rows(cflib):
+def test_prefill_agrees_with_decode_rows(cflib, consumer):
     """The decode kernel on the per-token rows gives the same answer (within
     twice the tolerance: each is within it of the truth)."""
     import torch
@@ -87,7 +96,7 @@ def test_prefill_agrees_with_decode_rows(cflib):
     assert bool((err <= 4e-3 + 2e-3 * out.double().abs()).all()), err.max().item()
 
 
-def test_prefill_ignores_garbage_past_context(cflib, oracle_mod):
+def test_prefill_ignores_garbage_past_context(cflib, oracle_mod, consumer):
     import torch
 
     from cacheflow_b200 import ops
@@ -107,7 +116,30 @@ def test_prefill_ignores_garbage_past_context(cflib, oracle_mod):
     assert_close(as_f64(out), want, "f16", "prefill with NaN past the context")
 
 
-def test_prefill_bad_block_id_is_recorded(cflib):
+@pytest.mark.parametrize("slope", [1 / 64, 1 / 256, -1 / 64])
+def test_prefill_scores_that_grow_along_the_context(cflib, oracle_mod, consumer, slope):
+    """Keys whose scores rise (or fall) steadily with position: the running row
+    maximum moves by about 16 (or 4) in log2 units per 64-key stage, which
+    exercises the deferred rescale of the output accumulator."""
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(11)
+    H, Hkv, D = 16, 4, 128
+    q, k, v, tables, ctx, qs = _case(rng, "f16", H, Hkv, D, [(0, 300), (500, 200), (37, 5)])
+    q = (1.0 + 0.05 * rng.standard_normal(q.shape)).astype(np.float16)
+    for c in range(len(ctx)):
+        pos = np.arange(int(ctx[c]))
+        b, o = tables[c][pos // 16], pos % 16
+        base = (slope * pos if slope > 0 else slope * (pos - ctx[c]))[:, None, None]
+        k[b, :, o, :] = (base + 0.05 * rng.standard_normal((len(pos), Hkv, D))).astype(np.float16)
+    out, _ = _run(ops, "f16", q, k, v, tables, ctx, qs)
+    rt, rc = _rows(tables, ctx, qs)
+    want = oracle_mod.paged_attention(q, k, v, rt, rc, 1 / math.sqrt(D), CODE["f16"], num_threads=8)
+    assert_close(as_f64(out), want, "f16", f"prefill, slope {slope}")
+    assert ops.device_errors(0) == 0
+
+
+def test_prefill_bad_block_id_is_recorded(cflib, consumer):
     from cacheflow_b200 import _lib, ops
 
     rng = np.random.default_rng(8)
