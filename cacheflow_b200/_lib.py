@@ -92,6 +92,20 @@ SIGNATURES = {
         [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_int32, c_void_p],
     ),
     "cf_paged_attention_v2_static_scratch": (c_int32, [POINTER(AttentionParams), c_void_p]),
+    "cf_paged_attention_append_v1": (
+        c_int32,
+        [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
+    ),
+    "cf_paged_attention_append_v2": (
+        c_int32,
+        [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int32, c_void_p],
+    ),
+    "cf_build_decode_inputs": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+         c_void_p],
+    ),
     "cf_paged_prefill_attention": (c_int32, [POINTER(PrefillParams), c_void_p]),
     "cf_reshape_and_cache": (
         c_int32,

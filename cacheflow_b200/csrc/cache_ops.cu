@@ -258,6 +258,71 @@ cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_list
   return check_launch();
 }
 
+// ---------------------------------------------------------------------------
+// Device-side decode-batch preparation: what the host loop of
+// BatchDecodeEngine::prepare_kv_cache_inputs (batch_decode.cpp:92-131) builds,
+// from one contiguous list of every row's block ids (CSR: row s owns
+// block_ids[block_offsets[s] .. block_offsets[s+1])):
+//   block_tables[s, b] = row s's b-th block id, 0 past its blocks (:98, :104-105)
+//   context_lens[s]    = positions[s] + 1                           (:103)
+//   slot_mapping[s]    = id of block positions[s] / bs * bs + positions[s] % bs
+//                        when the row has that block (:107-114), else -1
+//                        (the reference leaves it unset; -1 is the padding
+//                        slot that reshape_and_cache skips).
+// A negative position gives an empty row (context 0, slot -1).  A row with
+// more blocks than max_blocks_per_seq keeps the first max_blocks_per_seq
+// and records CF_DEVERR_CONTEXT_LEN; a slot past INT32_MAX records
+// CF_DEVERR_SLOT.  Grid (ceil(max_blocks_per_seq / 256), rows): one thread per
+// table entry, coalesced.
+// ---------------------------------------------------------------------------
+constexpr int kBuildThreads = 256;
+
+__global__ void __launch_bounds__(kBuildThreads)
+    build_decode_inputs_kernel(const int32_t* __restrict__ positions,
+                               const int64_t* __restrict__ block_offsets,
+                               const int32_t* __restrict__ block_ids, int32_t max_blocks,
+                               int32_t block_size, int32_t* __restrict__ block_tables,
+                               int32_t* __restrict__ context_lens,
+                               int32_t* __restrict__ slot_mapping) {
+  const int s = blockIdx.y;
+  const int64_t o0 = block_offsets[s];
+  const int64_t n = block_offsets[s + 1] - o0;
+  const int64_t lim = n < 0 ? 0 : (n < max_blocks ? n : max_blocks);
+  const int b = blockIdx.x * kBuildThreads + threadIdx.x;
+  if (b < max_blocks) block_tables[(size_t)s * max_blocks + b] = b < lim ? block_ids[o0 + b] : 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (n < 0 || n > max_blocks) cache_error(CF_DEVERR_CONTEXT_LEN);
+    const int32_t pos = positions[s];
+    int32_t slot = -1;
+    if (pos >= 0 && pos < INT32_MAX) {
+      context_lens[s] = pos + 1;
+      const int64_t bi = pos / block_size;
+      if (bi < lim) {
+        const int64_t v = (int64_t)block_ids[o0 + bi] * block_size + pos % block_size;
+        if (v >= 0 && v <= INT32_MAX)
+          slot = (int32_t)v;
+        else
+          cache_error(CF_DEVERR_SLOT);
+      }
+    } else {
+      context_lens[s] = 0;
+    }
+    slot_mapping[s] = slot;
+  }
+}
+
+cf_status launch_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                     const int32_t* block_ids, int32_t num_seqs,
+                                     int32_t max_blocks_per_seq, int32_t block_size,
+                                     int32_t* block_tables, int32_t* context_lens,
+                                     int32_t* slot_mapping, cudaStream_t stream) {
+  dim3 grid((unsigned)((max_blocks_per_seq + kBuildThreads - 1) / kBuildThreads), (unsigned)num_seqs);
+  build_decode_inputs_kernel<<<grid, kBuildThreads, 0, stream>>>(
+      positions, block_offsets, block_ids, max_blocks_per_seq, block_size, block_tables,
+      context_lens, slot_mapping);
+  return check_launch();
+}
+
 cf_status cache_ops_read_errors(uint32_t* bits, bool clear) {
   uint32_t v = 0;
   cf_status s = cuda_status(cudaMemcpyFromSymbol(&v, g_cache_errors, sizeof(v)));

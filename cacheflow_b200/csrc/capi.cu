@@ -101,6 +101,51 @@ cf_status check_attention_params(const cf_paged_attention_params* p, bool check_
   return CF_OK;
 }
 
+size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out);
+
+// cf_paged_attention_v1 / _append_v1 (key == nullptr: no append).
+cf_status run_v1(const cf_paged_attention_params* p, void* workspace, size_t workspace_bytes,
+                 void* stream, const void* key, const void* value, const int32_t* slots) {
+  cf_status st = check_attention_params(p);
+  if (st != CF_OK || p->num_seqs == 0) return st;
+  AttnLaunch l{p, 0, 1, nullptr, nullptr, nullptr, (cudaStream_t)stream};
+  l.new_k = key;
+  l.new_v = value;
+  l.slot_mapping = slots;
+  int32_t parts = 0;
+  const size_t need = v1_split_bytes(p, &parts);
+  if (need > 0 && workspace != nullptr && workspace_bytes >= need) {
+    if (!aligned16(workspace)) return CF_ERR_INVALID_ARGUMENT;
+    const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
+    const int64_t r4 = (rows * 4 + 255) / 256 * 256;
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    l.part_tokens = v1_split_tokens(p);
+    l.num_parts = parts;
+    l.part_max = reinterpret_cast<float*>(w);
+    l.part_sum = reinterpret_cast<float*>(w + r4);
+    l.part_out = reinterpret_cast<float*>(w + 2 * r4);
+  }
+  return launch_paged_attention(l);
+}
+
+// cf_paged_attention_v2 / _append_v2.
+cf_status run_v2(const cf_paged_attention_params* p, float* exp_sums, float* max_logits,
+                 float* tmp_output, int32_t num_partitions, void* stream, const void* key,
+                 const void* value, const int32_t* slots) {
+  cf_status st = check_attention_params(p);
+  if (st != CF_OK || p->num_seqs == 0) return st;
+  if (!exp_sums || !max_logits || !tmp_output || num_partitions < 1)
+    return CF_ERR_INVALID_ARGUMENT;
+  const int64_t need = ((int64_t)p->max_context_len + kV2PartitionTokens - 1) / kV2PartitionTokens;
+  if (need > num_partitions) return CF_ERR_WORKSPACE;
+  AttnLaunch l{p, kV2PartitionTokens, num_partitions, max_logits, exp_sums, tmp_output,
+               (cudaStream_t)stream};
+  l.new_k = key;
+  l.new_v = value;
+  l.slot_mapping = slots;
+  return launch_paged_attention(l);
+}
+
 size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out) {
   const int32_t split = v1_split_tokens(p);
   if (split <= 0 || p->num_seqs <= 0 || p->max_context_len <= split) return 0;
@@ -142,37 +187,49 @@ size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) 
 
 cf_status cf_paged_attention_v1(const cf_paged_attention_params* p, void* workspace,
                                 size_t workspace_bytes, void* stream) {
-  cf_status st = check_attention_params(p);
-  if (st != CF_OK || p->num_seqs == 0) return st;
-  AttnLaunch l{p, 0, 1, nullptr, nullptr, nullptr, (cudaStream_t)stream};
-  int32_t parts = 0;
-  const size_t need = v1_split_bytes(p, &parts);
-  if (need > 0 && workspace != nullptr && workspace_bytes >= need) {
-    if (!aligned16(workspace)) return CF_ERR_INVALID_ARGUMENT;
-    const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
-    const int64_t r4 = (rows * 4 + 255) / 256 * 256;
-    uint8_t* w = static_cast<uint8_t*>(workspace);
-    l.part_tokens = v1_split_tokens(p);
-    l.num_parts = parts;
-    l.part_max = reinterpret_cast<float*>(w);
-    l.part_sum = reinterpret_cast<float*>(w + r4);
-    l.part_out = reinterpret_cast<float*>(w + 2 * r4);
-  }
-  return launch_paged_attention(l);
+  return run_v1(p, workspace, workspace_bytes, stream, nullptr, nullptr, nullptr);
 }
 
 cf_status cf_paged_attention_v2(const cf_paged_attention_params* p, float* exp_sums,
                                 float* max_logits, float* tmp_output, int32_t num_partitions,
                                 void* stream) {
-  cf_status st = check_attention_params(p);
-  if (st != CF_OK || p->num_seqs == 0) return st;
-  if (!exp_sums || !max_logits || !tmp_output || num_partitions < 1)
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, nullptr, nullptr,
+                nullptr);
+}
+
+cf_status cf_paged_attention_append_v1(const cf_paged_attention_params* p, const void* key,
+                                       const void* value, const int32_t* slot_mapping,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  // The append writes the caches: block ids must be range-checked (num_blocks > 0).
+  if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
+  if (p && p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
+  return run_v1(p, workspace, workspace_bytes, stream, key, value, slot_mapping);
+}
+
+cf_status cf_paged_attention_append_v2(const cf_paged_attention_params* p, const void* key,
+                                       const void* value, const int32_t* slot_mapping,
+                                       float* exp_sums, float* max_logits, float* tmp_output,
+                                       int32_t num_partitions, void* stream) {
+  if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
+  if (p && p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, key, value,
+                slot_mapping);
+}
+
+cf_status cf_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                 const int32_t* block_ids, int32_t num_seqs,
+                                 int32_t max_blocks_per_seq, int32_t block_size,
+                                 int32_t* block_tables, int32_t* context_lens,
+                                 int32_t* slot_mapping, void* stream) {
+  if (num_seqs < 0 || max_blocks_per_seq < 1 || block_size <= 0) return CF_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0) return CF_OK;
+  if (num_seqs > 65535) return CF_ERR_UNSUPPORTED;
+  if (!positions || !block_offsets || !block_ids || !block_tables || !context_lens ||
+      !slot_mapping)
     return CF_ERR_INVALID_ARGUMENT;
-  const int64_t need = ((int64_t)p->max_context_len + kV2PartitionTokens - 1) / kV2PartitionTokens;
-  if (need > num_partitions) return CF_ERR_WORKSPACE;
-  AttnLaunch l{p, kV2PartitionTokens, num_partitions, max_logits, exp_sums, tmp_output,
-               (cudaStream_t)stream};
-  return launch_paged_attention(l);
+  return launch_build_decode_inputs(positions, block_offsets, block_ids, num_seqs,
+                                    max_blocks_per_seq, block_size, block_tables, context_lens,
+                                    slot_mapping, (cudaStream_t)stream);
 }
 
 cf_status cf_paged_prefill_attention(const cf_prefill_params* p, void* stream) {

@@ -33,6 +33,10 @@ struct AttnLaunch {
   float* part_sum;
   float* part_out;      // [num_seqs, num_heads, num_parts, head_dim]
   cudaStream_t stream;
+  // Fused append of each row's newest token (null new_k: attention only).
+  const void* new_k = nullptr;  // [num_seqs, num_kv_heads, head_dim]
+  const void* new_v = nullptr;
+  const int32_t* slot_mapping = nullptr;  // [num_seqs] or null
 };
 cf_status launch_paged_attention(const AttnLaunch& l);
 bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype);
@@ -61,6 +65,11 @@ cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t
                                int64_t num_blocks, cudaStream_t stream);
 cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_listed,
                                int64_t block_bytes, int64_t num_blocks, cudaStream_t stream);
+cf_status launch_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                     const int32_t* block_ids, int32_t num_seqs,
+                                     int32_t max_blocks_per_seq, int32_t block_size,
+                                     int32_t* block_tables, int32_t* context_lens,
+                                     int32_t* slot_mapping, cudaStream_t stream);
 cf_status cache_ops_read_errors(uint32_t* bits, bool clear);
 
 }  // namespace cfb

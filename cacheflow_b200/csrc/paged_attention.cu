@@ -69,6 +69,14 @@ struct AttnArgs {
   int32_t part_blocks;  // KV blocks per partition
   int32_t num_parts;    // partition stride of the scratch
   int64_t num_blocks;   // pool size (checked range of physical ids)
+  // Fused append (null new_k: none).  Row s's newest token -- position
+  // context_lens[s] - 1 -- takes its K/V from new_k/new_v[s, kvh, :] and is
+  // written to the cache at that position's slot.
+  const void* new_k;            // [S, Hkv, D]
+  const void* new_v;
+  const int32_t* slot_mapping;  // [S] or null (slot from the block table)
+  void* k_cache_w;              // the caches, written by the append
+  void* v_cache_w;
 };
 
 // ---------------------------------------------------------------------------
@@ -355,6 +363,51 @@ struct MmaConsumer {
 };
 
 // ---------------------------------------------------------------------------
+// Fused append: the warp that holds block `blk` (the one with the row's newest
+// token) in stage tile `kt` (K tile, then V tile) overwrites that token's row
+// with the new K/V -- in the tile's own layout: row-major for the FMA
+// consumer, 64-element boxes with the 128-byte swizzle for the MMA consumer --
+// and, for the CTA of head chunk 0 (`owner`), stores it into the cache, which
+// is what reshape_and_cache (kv_cache_kernels.cu:34-40) does with
+// slot = block_tables[s][blk] * 16 + (ctx - 1) % 16.  A slot_mapping entry
+// that is negative appends nothing; one that is not that slot is recorded
+// (CF_DEVERR_SLOT) and appends nothing.  Other CTAs of the same row may read
+// the cache row while it is written; they overwrite it in their own tile.
+// ---------------------------------------------------------------------------
+template <typename T, int D, bool kMma>
+__device__ __forceinline__ void append_token(const AttnArgs& a, uint8_t* kt, int seq, int kvh, int blk,
+                                             int ctx, bool owner, int lane) {
+  constexpr int kTile = kBlockTokens * D * (int)sizeof(T);
+  constexpr int kRowChunks = D * (int)sizeof(T) / 16;
+  constexpr int kVec = 16 / (int)sizeof(T);
+  const int tok = ctx - 1 - blk * kBlockTokens;
+  const int32_t phys = a.block_tables[(size_t)seq * a.max_blocks_per_seq + blk];
+  if (a.slot_mapping != nullptr) {
+    const int32_t slot = a.slot_mapping[seq];
+    if (slot < 0) return;
+    if ((int64_t)slot != (int64_t)phys * kBlockTokens + tok) {
+      if (owner && lane == 0) attn_error(CF_DEVERR_SLOT);
+      return;
+    }
+  }
+  const size_t src = ((size_t)seq * a.num_kv_heads + kvh) * D;
+  const size_t dst = (((size_t)phys * a.num_kv_heads + kvh) * kBlockTokens + tok) * D;
+  for (int i = lane; i < 2 * kRowChunks; i += 32) {
+    const int kv = i >= kRowChunks ? 1 : 0;
+    const int c = i - kv * kRowChunks;
+    const uint4 val =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(kv ? a.new_v : a.new_k) + src + c * kVec);
+    const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + tok * 128 + (((c & 7) ^ (tok & 7)) << 4)
+                         : tok * D * (int)sizeof(T) + c * 16;
+    *reinterpret_cast<uint4*>(kt + kv * kTile + off) = val;
+    if (owner)
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? a.v_cache_w : a.k_cache_w) + dst + c * kVec) = val;
+  }
+  fence_proxy_async_smem();  // a later TMA write of this tile follows these stores
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
 // Kernel configuration (per element type / head dim).
 // ---------------------------------------------------------------------------
 template <typename T, int D, int HG>
@@ -374,7 +427,7 @@ struct AttnConfig {
   static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
 };
 
-template <typename T, int D, int HG, bool kMma>
+template <typename T, int D, int HG, bool kMma, bool kAppend>
 __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     paged_attention_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv) {
@@ -404,6 +457,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
   if (part == 0 && nparts > (int)gridDim.x && threadIdx.x == 0 && blockIdx.y == 0)
     attn_error(CF_DEVERR_CONTEXT_LEN);  // context_lens exceeds max_context_len
   const bool single = (nparts == 1);
+  const int last_blk = (kAppend && ctx > 0) ? (ctx - 1) / kBlockTokens : -1;
   const int pb0 = part * a.part_blocks;
   const int pb1 = min(nblk, pb0 + a.part_blocks);
 
@@ -496,7 +550,10 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     const int blk = pb0 + warp + i * NW;
     const int ntok = min(kBlockTokens, ctx - blk * kBlockTokens);
     if (flags[s]) {
-      const uint8_t* kt = tiles + (size_t)s * 2 * TILE;
+      uint8_t* kt = tiles + (size_t)s * 2 * TILE;
+      if constexpr (kAppend) {
+        if (blk == last_blk) append_token<T, D, kMma>(a, kt, seq, kvh, blk, ctx, chunk == 0, lane);
+      }
       cons.block(kt, kt + TILE, ntok, pbuf, lane);
     }
     __syncwarp();
@@ -695,11 +752,11 @@ bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int3
 namespace {
 
 // Per kernel instantiation and device: opt in to > 48 KB of dynamic smem.
-template <typename T, int D, int HG, bool kMma>
+template <typename T, int D, int HG, bool kMma, bool kAppend>
 cf_status ensure_smem(int bytes) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
-  auto kern = paged_attention_kernel<T, D, HG, kMma>;
+  auto kern = paged_attention_kernel<T, D, HG, kMma, kAppend>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -715,15 +772,15 @@ struct Maps {
   CUtensorMap k, v;
 };
 
-template <typename T, int D, int HG, bool kMma>
+template <typename T, int D, int HG, bool kMma, bool kAppend>
 cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& maps) {
   using Cfg = AttnConfig<T, D, HG>;
   const cf_paged_attention_params& p = *l.p;
   a.head_chunks = (a.group + HG - 1) / HG;
-  cf_status st = ensure_smem<T, D, HG, kMma>(Cfg::kSmemAlloc);
+  cf_status st = ensure_smem<T, D, HG, kMma, kAppend>(Cfg::kSmemAlloc);
   if (st != CF_OK) return st;
   dim3 grid((unsigned)grid_x, (unsigned)(p.num_kv_heads * a.head_chunks), (unsigned)p.num_seqs);
-  paged_attention_kernel<T, D, HG, kMma>
+  paged_attention_kernel<T, D, HG, kMma, kAppend>
       <<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a, maps.k, maps.v);
   st = check_launch();
   if (st != CF_OK || l.part_max == nullptr || grid_x == 1) return st;
@@ -766,7 +823,7 @@ bool use_mma(const cf_paged_attention_params& p, int64_t rows) {
   return p.num_heads / p.num_kv_heads >= 3;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kAppend>
 cf_status launch_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
   const cf_paged_attention_params& p = *l.p;
   Maps maps;
@@ -775,23 +832,29 @@ cf_status launch_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
     const int64_t rows = p.num_blocks * (int64_t)p.num_kv_heads * kBlockTokens;
     if (use_mma(p, rows) && kv_tensor_map(&maps.k, p.key_cache, rows, D, p.dtype) &&
         kv_tensor_map(&maps.v, p.value_cache, rows, D, p.dtype))
-      return launch_typed<T, D, 8, true>(l, a, grid_x, maps);
+      return launch_typed<T, D, 8, true, kAppend>(l, a, grid_x, maps);
   }
-  if (a.group == 1) return launch_typed<T, D, 1, false>(l, a, grid_x, maps);
-  if (a.group == 2) return launch_typed<T, D, 2, false>(l, a, grid_x, maps);
-  return launch_typed<T, D, 4, false>(l, a, grid_x, maps);
+  if (a.group == 1) return launch_typed<T, D, 1, false, kAppend>(l, a, grid_x, maps);
+  if (a.group == 2) return launch_typed<T, D, 2, false, kAppend>(l, a, grid_x, maps);
+  return launch_typed<T, D, 4, false, kAppend>(l, a, grid_x, maps);
+}
+
+template <typename T, bool kAppend>
+cf_status launch_head_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
+  switch (l.p->head_dim) {
+    case 64: return launch_dim<T, 64, kAppend>(l, a, grid_x);
+    case 128: return launch_dim<T, 128, kAppend>(l, a, grid_x);
+    case 256:
+      if constexpr (sizeof(T) == 2) return launch_dim<T, 256, kAppend>(l, a, grid_x);
+      return CF_ERR_UNSUPPORTED;
+    default: return CF_ERR_UNSUPPORTED;
+  }
 }
 
 template <typename T>
 cf_status launch_type(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
-  switch (l.p->head_dim) {
-    case 64: return launch_dim<T, 64>(l, a, grid_x);
-    case 128: return launch_dim<T, 128>(l, a, grid_x);
-    case 256:
-      if constexpr (sizeof(T) == 2) return launch_dim<T, 256>(l, a, grid_x);
-      return CF_ERR_UNSUPPORTED;
-    default: return CF_ERR_UNSUPPORTED;
-  }
+  return a.new_k != nullptr ? launch_head_dim<T, true>(l, a, grid_x)
+                            : launch_head_dim<T, false>(l, a, grid_x);
 }
 
 }  // namespace
@@ -824,6 +887,11 @@ cf_status launch_paged_attention(const AttnLaunch& l) {
   a.head_chunks = 1;
   a.max_blocks_per_seq = p.max_blocks_per_seq;
   a.num_blocks = p.num_blocks > 0 ? p.num_blocks : INT64_MAX;
+  a.new_k = l.new_k;
+  a.new_v = l.new_v;
+  a.slot_mapping = l.slot_mapping;
+  a.k_cache_w = const_cast<void*>(p.key_cache);
+  a.v_cache_w = const_cast<void*>(p.value_cache);
   int grid_x = 1;
   if (l.part_tokens > 0 && l.part_max != nullptr) {
     a.part_blocks = l.part_tokens / kBlockTokens;

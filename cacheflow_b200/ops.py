@@ -153,6 +153,96 @@ def paged_attention_v2(out, exp_sums, max_logits, tmp_output, query, key_cache, 
     return out
 
 
+def _check_new_rows(key, value, query, key_cache):
+    want = (query.shape[0], key_cache.shape[1], key_cache.shape[3])
+    for name, t in (("key", key), ("value", value)):
+        if tuple(t.shape) != want or t.dtype != key_cache.dtype or not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT,
+                                 f"{name} must be contiguous {key_cache.dtype} of shape {want}")
+
+
+def paged_attention_append_v1(out, query, key, value, key_cache, value_cache, block_tables, context_lens,
+                              slot_mapping=None, scale=None, max_context_len=None,
+                              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused decode step: reshape_and_cache of every row's newest token (at
+    position context_lens[s] - 1) followed by paged_attention_v1, in one launch.
+
+    key/value: [num_seqs, num_kv_heads, head_dim]; slot_mapping: int32 [num_seqs]
+    or None (the slot comes from the block table).  Writes key_cache/value_cache.
+    """
+    lib = _lib.load()
+    _check_new_rows(key, value, query, key_cache)
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len)
+    ws = _ptr(workspace)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib.cf_paged_attention_append_v1(ctypes.byref(p), _ptr(key), _ptr(value), _ptr(slot_mapping),
+                                           ws, ws_bytes, _stream(query)),
+          "cf_paged_attention_append_v1")
+    return out
+
+
+def paged_attention_append_v2(out, exp_sums, max_logits, tmp_output, query, key, value, key_cache,
+                              value_cache, block_tables, context_lens, slot_mapping=None, scale=None,
+                              max_context_len=None) -> torch.Tensor:
+    """Fused decode step on the partitioned path: reshape_and_cache of every
+    row's newest token followed by paged_attention_v2, in one partition launch
+    (+ the reduce)."""
+    lib = _lib.load()
+    _check_new_rows(key, value, query, key_cache)
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len)
+    for t in (exp_sums, max_logits, tmp_output):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "v2 scratch must be contiguous float32")
+    check(lib.cf_paged_attention_append_v2(ctypes.byref(p), _ptr(key), _ptr(value), _ptr(slot_mapping),
+                                           _ptr(exp_sums), _ptr(max_logits), _ptr(tmp_output),
+                                           exp_sums.shape[-1], _stream(query)),
+          "cf_paged_attention_append_v2")
+    return out
+
+
+def build_decode_inputs(positions, block_offsets, block_ids, max_blocks_per_seq, block_size=16,
+                        block_tables=None, context_lens=None, slot_mapping=None):
+    """Device-side prepare_kv_cache_inputs (batch_decode.cpp:92-131).
+
+    positions: int32 [S]; block_offsets: int64 [S + 1]; block_ids: int32 (row s
+    owns block_ids[block_offsets[s]:block_offsets[s + 1]]).  Returns
+    (block_tables int32 [S, max_blocks_per_seq], context_lens int32 [S],
+    slot_mapping int32 [S]), allocated when not given.
+    """
+    lib = _lib.load()
+    S = positions.shape[0]
+    dev = positions.device
+    for name, t, dt in (("positions", positions, torch.int32), ("block_offsets", block_offsets, torch.int64),
+                        ("block_ids", block_ids, torch.int32)):
+        if t.dtype != dt or not t.is_contiguous() or t.device != dev:
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, f"{name} must be contiguous {dt} on {dev}")
+    if block_offsets.shape[0] != S + 1:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "block_offsets must have num_seqs + 1 entries")
+    if block_tables is None:
+        block_tables = torch.empty((S, max_blocks_per_seq), dtype=torch.int32, device=dev)
+    if context_lens is None:
+        context_lens = torch.empty((S,), dtype=torch.int32, device=dev)
+    if slot_mapping is None:
+        slot_mapping = torch.empty((S,), dtype=torch.int32, device=dev)
+    if block_ids.numel() == 0:
+        block_ids = torch.zeros((1,), dtype=torch.int32, device=dev)
+    check(lib.cf_build_decode_inputs(_ptr(positions), _ptr(block_offsets), _ptr(block_ids), S,
+                                     int(max_blocks_per_seq), int(block_size), _ptr(block_tables),
+                                     _ptr(context_lens), _ptr(slot_mapping), _stream(positions)),
+          "cf_build_decode_inputs")
+    return block_tables, context_lens, slot_mapping
+
+
 def paged_prefill_attention(out, query, key_cache, value_cache, block_tables, context_lens, query_start,
                             scale=None, max_query_len=None) -> torch.Tensor:
     """Chunked-prefill attention (no CacheFlow counterpart).

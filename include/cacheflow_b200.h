@@ -107,6 +107,59 @@ CF_API cf_status cf_paged_attention_v2(const cf_paged_attention_params* params,
                                 float* tmp_output, int32_t num_partitions,
                                 void* stream);
 
+/* Fused decode step: appends every row's newest token to the cache and
+ * attends, in one launch.  Equal to cf_reshape_and_cache(key, value,
+ * key_cache, value_cache, slot_mapping, num_tokens = num_seqs, ...) followed by
+ * cf_paged_attention_v1 (same workspace rules) on `params`, for batches in
+ * which row s's new token sits at position context_lens[s] - 1 (it is already
+ * counted in context_lens, as in CacheFlow's prepare_kv_cache_inputs,
+ * batch_decode.cpp:103-114).  Replaces the pair
+ * cacheflow::cuda::launch_reshape_and_cache (kv_cache_kernels.cuh:17-27) +
+ * launch_paged_attention_v1 (paged_attention.cuh:44-46) that
+ * BatchDecodeEngine issues per step.
+ *   key, value    [num_seqs, num_kv_heads, head_dim] of params->dtype, 16-byte
+ *                 aligned: the new token of each row.
+ *   slot_mapping  [num_seqs] or NULL.  NULL: the slot is the one the block
+ *                 table gives position context_lens[s] - 1.  An entry < 0:
+ *                 row s appends nothing.  An entry >= 0 must equal that slot;
+ *                 otherwise CF_DEVERR_SLOT is recorded and the row appends
+ *                 nothing.
+ * params->key_cache / value_cache are WRITTEN (the appended rows), so
+ * params->num_blocks must be the pool size (> 0).  No row may
+ * read a slot that another row appends in the same call (a sequence appends
+ * into its own last block; copy-on-write forks run before, as in CacheFlow's
+ * scheduler).  Rows with context 0 append nothing. */
+CF_API cf_status cf_paged_attention_append_v1(const cf_paged_attention_params* params,
+                                              const void* key, const void* value,
+                                              const int32_t* slot_mapping, void* workspace,
+                                              size_t workspace_bytes, void* stream);
+
+/* The same fused step on the partitioned path: cf_reshape_and_cache followed
+ * by cf_paged_attention_v2 (same scratch rules).  Replaces
+ * launch_reshape_and_cache + launch_paged_attention_v2 (paged_attention.cuh:48-54). */
+CF_API cf_status cf_paged_attention_append_v2(const cf_paged_attention_params* params,
+                                              const void* key, const void* value,
+                                              const int32_t* slot_mapping, float* exp_sums,
+                                              float* max_logits, float* tmp_output,
+                                              int32_t num_partitions, void* stream);
+
+/* Device-side batch preparation.  Builds, on the device, what CacheFlow's
+ * BatchDecodeEngine::prepare_kv_cache_inputs (batch_decode.cpp:92-131) builds
+ * on the host each step, from every row's block ids in one contiguous list:
+ * row s owns block_ids[block_offsets[s] .. block_offsets[s + 1]).
+ *   block_tables [num_seqs, max_blocks_per_seq]: the row's ids, then 0
+ *   context_lens [num_seqs]: positions[s] + 1 (0 for a negative position)
+ *   slot_mapping [num_seqs]: the slot of position positions[s], or -1 when the
+ *                row has no block for it (the reference leaves it unset)
+ * block_offsets is int64 [num_seqs + 1].  A row with more than
+ * max_blocks_per_seq ids keeps the first ones and records
+ * CF_DEVERR_CONTEXT_LEN. */
+CF_API cf_status cf_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                        const int32_t* block_ids, int32_t num_seqs,
+                                        int32_t max_blocks_per_seq, int32_t block_size,
+                                        int32_t* block_tables, int32_t* context_lens,
+                                        int32_t* slot_mapping, void* stream);
+
 /* Parameters of one chunked-prefill attention call.  Chunk c owns query
  * tokens [query_start[c], query_start[c+1]) (its chunk length n_c) and a
  * sequence whose first context_lens[c] tokens are in the cache, the chunk's

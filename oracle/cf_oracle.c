@@ -269,3 +269,37 @@ void cfo_memset_blocks(void* cache, const int32_t* block_ids, int32_t num_listed
   for (int i = 0; i < num_listed; ++i)
     memset((char*)cache + (int64_t)block_ids[i] * block_bytes, 0, (size_t)block_bytes);
 }
+
+/* batch_decode.cpp:96-99: tables zero-initialised to the widest row;
+ * :103 context length = position + 1; :104-105 ids copied in order;
+ * :107-114 slot = table[position / bs] * bs + position % bs when the row has
+ * that block.  A negative position (never produced by the reference) is an
+ * empty row here. */
+int32_t cfo_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                const int32_t* block_ids, int32_t num_seqs,
+                                int32_t max_blocks_per_seq, int32_t block_size,
+                                int32_t* block_tables, int32_t* context_lens,
+                                int32_t* slot_mapping) {
+  int32_t cut = 0;
+  for (int32_t s = 0; s < num_seqs; ++s) {
+    const int64_t n = block_offsets[s + 1] - block_offsets[s];
+    const int64_t keep = n < 0 ? 0 : (n < max_blocks_per_seq ? n : max_blocks_per_seq);
+    if (n < 0 || n > max_blocks_per_seq) ++cut;
+    int32_t* row = block_tables + (int64_t)s * max_blocks_per_seq;
+    for (int64_t b = 0; b < max_blocks_per_seq; ++b)
+      row[b] = b < keep ? block_ids[block_offsets[s] + b] : 0;
+    const int32_t pos = positions[s];
+    slot_mapping[s] = -1;
+    if (pos < 0 || pos == INT32_MAX) {
+      context_lens[s] = 0;
+      continue;
+    }
+    context_lens[s] = pos + 1;
+    const int64_t bi = pos / block_size;
+    if (bi < keep) {
+      const int64_t v = (int64_t)row[bi] * block_size + pos % block_size;
+      if (v >= 0 && v <= INT32_MAX) slot_mapping[s] = (int32_t)v;
+    }
+  }
+  return cut;
+}

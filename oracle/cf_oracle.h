@@ -65,6 +65,19 @@ void cfo_compact_kv_cache(void* key_cache, void* value_cache, const int32_t* src
 void cfo_memset_blocks(void* cache, const int32_t* block_ids, int32_t num_listed,
                        int64_t block_bytes);
 
+/* Decode-batch preparation of BatchDecodeEngine::prepare_kv_cache_inputs
+ * (batch_decode.cpp:92-131), rows given as CSR block lists: row s at
+ * positions[s] owns block_ids[block_offsets[s] .. block_offsets[s+1]).
+ * Writes block_tables [num_seqs, max_blocks_per_seq] (ids, then 0),
+ * context_lens = position + 1 (0 for a negative position) and slot_mapping
+ * (-1 where the reference leaves the slot unset); rows longer than
+ * max_blocks_per_seq are cut.  Returns the number of cut rows. */
+int32_t cfo_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,
+                                const int32_t* block_ids, int32_t num_seqs,
+                                int32_t max_blocks_per_seq, int32_t block_size,
+                                int32_t* block_tables, int32_t* context_lens,
+                                int32_t* slot_mapping);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,9 @@ def lib() -> ctypes.CDLL:
         L.cfo_swap_blocks.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int64]
         L.cfo_compact_kv_cache.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64]
         L.cfo_memset_blocks.argtypes = [c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_build_decode_inputs.restype = c_int32
+        L.cfo_build_decode_inputs.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                              c_void_p, c_void_p, c_void_p]
         L.cfo_load.restype = c_double
         L.cfo_load.argtypes = [c_void_p, c_int64, c_int32]
         _LIB = L
@@ -141,6 +144,22 @@ def memset_blocks(cache, block_ids) -> None:
     lib().cfo_memset_blocks(_p(cache), _p(b), b.shape[0], cache[0].nbytes)
 
 
+def build_decode_inputs(positions, block_offsets, block_ids, max_blocks_per_seq, block_size=16):
+    """(block_tables, context_lens, slot_mapping, rows cut) of prepare_kv_cache_inputs."""
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    off = np.ascontiguousarray(block_offsets, dtype=np.int64)
+    ids = np.ascontiguousarray(block_ids, dtype=np.int32)
+    if ids.size == 0:
+        ids = np.zeros(1, np.int32)
+    S = pos.shape[0]
+    tables = np.zeros((S, max_blocks_per_seq), np.int32)
+    ctx = np.zeros(S, np.int32)
+    slots = np.zeros(S, np.int32)
+    cut = lib().cfo_build_decode_inputs(_p(pos), _p(off), _p(ids), S, max_blocks_per_seq, block_size,
+                                        _p(tables), _p(ctx), _p(slots))
+    return tables, ctx, slots, int(cut)
+
+
 # ---------------------------------------------------------------------------
 # numpy restatement of the attention math (independent second restatement,
 # used to cross-check the C oracle on small cases).
@@ -212,6 +231,9 @@ class RefCpu:
         L.refcpu_step.restype = c_double
         L.refcpu_step.argtypes = [c_void_p]
         L.refcpu_destroy.argtypes = [c_void_p]
+        L.refcpu_prepare_inputs.restype = c_int32
+        L.refcpu_prepare_inputs.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_void_p,
+                                            c_void_p, c_void_p, c_void_p]
         self.lib = L
         self.shape = (num_blocks, num_kv_heads, 16, head_dim)
         self.h = L.refcpu_create(num_heads, num_kv_heads, head_dim, num_blocks, num_threads)
@@ -230,6 +252,24 @@ class RefCpu:
 
     def step(self) -> float:
         return float(self.lib.refcpu_step(self.h))
+
+    def prepare_inputs(self, positions, block_offsets, block_ids):
+        """The reference's prepare_kv_cache_inputs on CSR rows: (tables, context_lens, slots)."""
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        off = np.ascontiguousarray(block_offsets, dtype=np.int64)
+        ids = np.ascontiguousarray(block_ids, dtype=np.int32)
+        if ids.size == 0:
+            ids = np.zeros(1, np.int32)
+        S = pos.shape[0]
+        cap = int(np.diff(off).max()) if S else 0
+        tables = np.zeros((S, max(cap, 1)), np.int32)
+        ctx = np.zeros(S, np.int32)
+        slots = np.zeros(S, np.int32)
+        mb = c_int32(0)
+        rc = self.lib.refcpu_prepare_inputs(self.h, S, _p(pos), _p(off), _p(ids), tables.shape[1], _p(tables),
+                                            ctypes.byref(mb), _p(ctx), _p(slots))
+        assert rc == 0
+        return tables.reshape(-1)[: S * mb.value].reshape(S, mb.value), ctx, slots
 
     def close(self) -> None:
         if self.h:

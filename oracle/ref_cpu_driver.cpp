@@ -105,4 +105,45 @@ REF_API double refcpu_step(void* h) {
   return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 
+// Runs the reference's own BatchDecodeEngine::prepare_kv_cache_inputs
+// (batch_decode.cpp:92-131) on a batch whose row s is at `positions[s]` and
+// owns block_ids[block_offsets[s] .. block_offsets[s+1]); copies out its
+// block tables ([num_seqs, *max_blocks_out], zero-padded by the reference),
+// context lengths and slot mapping.  `tables_out` has room for
+// num_seqs * tables_capacity entries; returns -1 if the tables do not fit.
+// Slots the reference leaves unset (position past the row's blocks) hold
+// whatever its uninitialised array held: the caller masks them.
+REF_API int32_t refcpu_prepare_inputs(void* h, int32_t num_seqs, const int32_t* positions,
+                                      const int64_t* block_offsets, const int32_t* block_ids,
+                                      int32_t tables_capacity, int32_t* tables_out,
+                                      int32_t* max_blocks_out, int32_t* context_lens_out,
+                                      int32_t* slot_mapping_out) {
+  auto* r = static_cast<RefCpu*>(h);
+  cacheflow::DecodeBatch batch;
+  for (int32_t s = 0; s < num_seqs; ++s) {
+    std::vector<cacheflow::BlockId> table(block_ids + block_offsets[s], block_ids + block_offsets[s + 1]);
+    batch.add((cacheflow::SeqId)s, 0, positions[s], std::move(table), false);
+  }
+  cacheflow::DecodeContext ctx;
+  r->engines[0]->prepare_kv_cache_inputs(batch, ctx);
+  size_t max_blocks = 0;
+  for (auto& e : batch.entries) max_blocks = std::max(max_blocks, e.block_table.size());
+  *max_blocks_out = (int32_t)max_blocks;
+  int32_t rc = 0;
+  if ((int64_t)max_blocks > tables_capacity) {
+    rc = -1;
+  } else {
+    for (int32_t s = 0; s < num_seqs; ++s) {
+      for (size_t b = 0; b < max_blocks; ++b)
+        tables_out[(size_t)s * max_blocks + b] = ctx.block_tables[(size_t)s * max_blocks + b];
+      context_lens_out[s] = ctx.context_lens[s];
+      slot_mapping_out[s] = ctx.slot_mapping[s];
+    }
+  }
+  delete[] ctx.block_tables;
+  delete[] ctx.context_lens;
+  delete[] ctx.slot_mapping;
+  return rc;
+}
+
 REF_API void refcpu_destroy(void* h) { delete static_cast<RefCpu*>(h); }

@@ -118,6 +118,22 @@ def test_invalid_arguments_rejected_without_gpu(cflib):
         _lib.CF_ERR_INVALID_ARGUMENT
     assert cflib.cf_memset_blocks(None, None, 0, 4096, 10, None) == _lib.CF_OK
     assert cflib.cf_status_string(_lib.CF_ERR_PLAN) == b"block-move plan would race"
+    # fused append: the new rows are required and 16-byte aligned
+    assert cflib.cf_paged_attention_append_v1(ctypes.byref(p), None, None, None, None, 0, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_paged_attention_append_v2(ctypes.byref(p), (1 << 20) + 8, 1 << 20, None, es, es, es, 1,
+                                              None) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_paged_attention_append_v2(ctypes.byref(p), 1 << 20, 1 << 20, None, es, es, es, 1, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT  # num_blocks 0: the appended ids could not be range-checked
+    p.num_blocks = 64
+    assert cflib.cf_paged_attention_append_v2(ctypes.byref(p), 1 << 20, 1 << 20, None, es, es, es, 1, None) == \
+        _lib.CF_ERR_WORKSPACE
+    # decode-input builder
+    assert cflib.cf_build_decode_inputs(None, None, None, 0, 4, 16, None, None, None, None) == _lib.CF_OK
+    assert cflib.cf_build_decode_inputs(None, None, None, 3, 4, 16, None, None, None, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_build_decode_inputs(None, None, None, 3, 0, 16, None, None, None, None) == \
+        _lib.CF_ERR_INVALID_ARGUMENT
 
 
 def test_compaction_planner_packs_without_overlap(cflib):

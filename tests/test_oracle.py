@@ -169,7 +169,8 @@ GOLDEN_FILES = sorted(GOLDEN.glob("*.npz"))
 @pytest.mark.parametrize("path", GOLDEN_FILES, ids=lambda p: p.stem)
 def test_oracle_reproduces_golden_vectors(oracle_mod, path):
     """Golden outputs were produced by CacheFlow's own CUDA kernels
-    (tests/golden/make_golden.py); the oracle must reproduce them."""
+    (tests/golden/make_golden.py) and its own host code
+    (tests/golden/make_golden_cpu.py); the oracle must reproduce them."""
     g = dict(np.load(path))
     op = str(g["op"])
     if op == "paged_attention_v1":
@@ -192,9 +193,30 @@ def test_oracle_reproduces_golden_vectors(oracle_mod, path):
         kc, vc = g["k_cache"].copy(), g["v_cache"].copy()
         oracle_mod.compact_kv_cache(kc, vc, g["src_ids"], g["dst_ids"])
         assert np.array_equal(kc, g["k_out"]) and np.array_equal(vc, g["v_out"])
+    elif op == "build_decode_inputs":
+        tables, ctx, slots, cut = oracle_mod.build_decode_inputs(
+            g["positions"], g["block_offsets"], g["block_ids"], g["block_tables"].shape[1])
+        assert cut == 0
+        assert np.array_equal(tables, g["block_tables"]) and np.array_equal(ctx, g["context_lens"])
+        assert np.array_equal(slots, g["slot_mapping"])
+        assert np.all(slots[~g["slot_set"]] == -1)
     elif op == "memset_blocks":
         c = g["cache"].copy()
         oracle_mod.memset_blocks(c, g["block_ids"])
         assert np.array_equal(c, g["out"])
     else:
         pytest.fail(f"unknown golden op {op}")
+
+
+def test_build_decode_inputs_edge_cases(oracle_mod):
+    """Negative positions are empty rows; rows longer than the table width are
+    cut (and counted); a position past the row's blocks gets slot -1."""
+    pos = np.array([-1, 0, 40, 5, 100], np.int32)
+    nblk = np.array([2, 1, 3, 6, 2], np.int64)
+    off = np.concatenate([[0], np.cumsum(nblk)]).astype(np.int64)
+    ids = np.arange(100, 100 + int(off[-1]), dtype=np.int32)
+    tables, ctx, slots, cut = oracle_mod.build_decode_inputs(pos, off, ids, 4)
+    assert cut == 1
+    assert ctx.tolist() == [0, 1, 41, 6, 101]
+    assert slots.tolist() == [-1, 102 * 16, 105 * 16 + 8, 106 * 16 + 5, -1]
+    assert tables[3].tolist() == [106, 107, 108, 109] and tables[1].tolist() == [102, 0, 0, 0]
