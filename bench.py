@@ -250,8 +250,12 @@ def run_ours(args):
 
     chunked = w.has_chunks and args.prefill == "chunked"
     nc = len(w.chunk_context_lens) if chunked else 0
+    # decode-only batches (one new token per row, at its newest position)
+    # append it inside the attention launch unless --append separate
+    fused = args.append == "fused" and not w.has_chunks and T == S
+    new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
-                          max_chunks=nc)
+                          max_chunks=nc, fused_append=fused)
     engine.q[:S].copy_(q)
     engine.tables.copy_(tables)
     engine.ctx.copy_(ctx)
@@ -278,21 +282,22 @@ def run_ours(args):
     def step(record=False):
         if pairs is not None:
             ops.copy_blocks(k_cache, v_cache, pairs)
-        ops.reshape_and_cache(k_new, v_new, k_cache, v_cache, slots)
+        if not fused:
+            ops.reshape_and_cache(k_new, v_new, k_cache, v_cache, slots)
         if record:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            engine.attend(S, mctx, chunks)
+            engine.attend(S, mctx, chunks, new_rows)
             b.record(stream)
             att_ev.append((a, b))
         else:
-            engine.attend(S, mctx, chunks)
+            engine.attend(S, mctx, chunks, new_rows)
 
     launches_per_step = None
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step()
-        launches_per_step = engine.launches_per_step + 1 + (1 if pairs is not None else 0)
+        launches_per_step = engine.launches_per_step + (0 if fused else 1) + (1 if pairs is not None else 0)
         torch.cuda.synchronize(dev)
         if ops.device_errors(local) != 0:
             raise RuntimeError("device error word set during warm-up")
@@ -389,6 +394,8 @@ def run_ours(args):
     if rank == 0:
         peak, peak_kind = hbm_peak()
         alg_bytes = kv_step + w.qo_bytes() + w.table_bytes()
+        if fused:  # the appended rows: new K/V read, cache rows written, slots read
+            alg_bytes += 2 * 2 * T * Hkv * D * k_cache.element_size() + 4 * T
         achieved = alg_bytes / (att_ms * 1e-3) / 1e9
         value = kv_total / (ms_step * 1e-3) / 1e9
         line = {
@@ -420,6 +427,8 @@ def run_ours(args):
                             ("one decode row per prefill token" if w.has_chunks else None)),
                 "attention": "v1" if mctx <= 8192 else "v2",
                 "v1_split": args.v1_split,
+                "append": ("new K/V appended inside the attention launch" if fused
+                           else "reshape_and_cache launch before attention"),
                 "l2": ("L2 flushed before every timed step (512 MB write, outside the step's events)"
                        if flush is not None else
                        "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (w.kv_bytes() / 1e9)),
@@ -576,6 +585,9 @@ def main():
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--append", choices=["fused", "separate"], default="fused",
+                    help="decode batches: append the new K/V inside the attention launch, or run "
+                         "reshape_and_cache before it")
     ap.add_argument("--prefill", choices=["chunked", "rows"], default="chunked",
                     help="prefill tokens of mixed batches: multi-query chunks or one decode row each")
     ap.add_argument("--swap-gb", type=float, default=4.0, help="GB swapped out and in (whole job)")

@@ -363,49 +363,76 @@ struct MmaConsumer {
 };
 
 // ---------------------------------------------------------------------------
-// Fused append: the warp that holds block `blk` (the one with the row's newest
-// token) in stage tile `kt` (K tile, then V tile) overwrites that token's row
-// with the new K/V -- in the tile's own layout: row-major for the FMA
-// consumer, 64-element boxes with the 128-byte swizzle for the MMA consumer --
-// and, for the CTA of head chunk 0 (`owner`), stores it into the cache, which
-// is what reshape_and_cache (kv_cache_kernels.cu:34-40) does with
-// slot = block_tables[s][blk] * 16 + (ctx - 1) % 16.  A slot_mapping entry
-// that is negative appends nothing; one that is not that slot is recorded
-// (CF_DEVERR_SLOT) and appends nothing.  Other CTAs of the same row may read
-// the cache row while it is written; they overwrite it in their own tile.
+// Fused append: the warp that will hold block `blk` (the one with the row's
+// newest token) loads the new K/V row, the block id and the slot before its
+// pipeline starts (so the patch waits on nothing); when that block's tile
+// lands it overwrites the token's row in the tile -- in the tile's own layout:
+// row-major for the FMA consumer, 64-element boxes with the 128-byte swizzle
+// for the MMA consumer -- and, in the CTA of head chunk 0 (`owner`), stores it
+// into the cache, which is what reshape_and_cache (kv_cache_kernels.cu:34-40)
+// does with slot = block_tables[s][blk] * 16 + (ctx - 1) % 16.  A slot_mapping
+// entry that is negative appends nothing; one that is not that slot is
+// recorded (CF_DEVERR_SLOT) and appends nothing.  Other CTAs of the same row
+// may read the cache row while it is written; they overwrite it in their own
+// tile.
 // ---------------------------------------------------------------------------
-template <typename T, int D, bool kMma>
-__device__ __forceinline__ void append_token(const AttnArgs& a, uint8_t* kt, int seq, int kvh, int blk,
-                                             int ctx, bool owner, int lane) {
-  constexpr int kTile = kBlockTokens * D * (int)sizeof(T);
-  constexpr int kRowChunks = D * (int)sizeof(T) / 16;
-  constexpr int kVec = 16 / (int)sizeof(T);
-  const int tok = ctx - 1 - blk * kBlockTokens;
-  const int32_t phys = a.block_tables[(size_t)seq * a.max_blocks_per_seq + blk];
-  if (a.slot_mapping != nullptr) {
-    const int32_t slot = a.slot_mapping[seq];
-    if (slot < 0) return;
-    if ((int64_t)slot != (int64_t)phys * kBlockTokens + tok) {
-      if (owner && lane == 0) attn_error(CF_DEVERR_SLOT);
-      return;
+template <typename T, int D>
+struct AppendRow {
+  static constexpr int kRowChunks = D * (int)sizeof(T) / 16;  // 16-byte chunks of one row
+  static constexpr int kPerLane = (2 * kRowChunks + 31) / 32;  // K then V
+  static constexpr int kVec = 16 / (int)sizeof(T);
+  uint4 v[kPerLane];
+  int32_t phys;
+  int32_t slot;  // slot_mapping[seq] (unused without a slot_mapping)
+  int tok;
+
+  // Issues the loads only: nothing here waits for them, so the warp's copy
+  // pipeline starts at once and the values arrive while it streams.
+  __device__ __forceinline__ void load(const AttnArgs& a, int seq, int kvh, int blk, int ctx, int lane) {
+    tok = ctx - 1 - blk * kBlockTokens;
+    phys = a.block_tables[(size_t)seq * a.max_blocks_per_seq + blk];
+    slot = a.slot_mapping != nullptr ? a.slot_mapping[seq] : 0;
+    const size_t src = ((size_t)seq * a.num_kv_heads + kvh) * D;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int i = lane + 32 * j;
+      if (i < 2 * kRowChunks) {
+        const int kv = i >= kRowChunks ? 1 : 0;
+        const int c = i - kv * kRowChunks;
+        v[j] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(kv ? a.new_v : a.new_k) + src +
+                                               c * kVec);
+      }
     }
   }
-  const size_t src = ((size_t)seq * a.num_kv_heads + kvh) * D;
-  const size_t dst = (((size_t)phys * a.num_kv_heads + kvh) * kBlockTokens + tok) * D;
-  for (int i = lane; i < 2 * kRowChunks; i += 32) {
-    const int kv = i >= kRowChunks ? 1 : 0;
-    const int c = i - kv * kRowChunks;
-    const uint4 val =
-        *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(kv ? a.new_v : a.new_k) + src + c * kVec);
-    const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + tok * 128 + (((c & 7) ^ (tok & 7)) << 4)
-                         : tok * D * (int)sizeof(T) + c * 16;
-    *reinterpret_cast<uint4*>(kt + kv * kTile + off) = val;
-    if (owner)
-      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? a.v_cache_w : a.k_cache_w) + dst + c * kVec) = val;
+
+  template <bool kMma>
+  __device__ __forceinline__ void patch(const AttnArgs& a, uint8_t* kt, int kvh, bool owner, int lane) const {
+    constexpr int kTile = kBlockTokens * D * (int)sizeof(T);
+    if (a.slot_mapping != nullptr) {
+      if (slot < 0) return;
+      if ((int64_t)slot != (int64_t)phys * kBlockTokens + tok) {
+        if (owner && lane == 0) attn_error(CF_DEVERR_SLOT);
+        return;
+      }
+    }
+    const size_t dst = (((size_t)phys * a.num_kv_heads + kvh) * kBlockTokens + tok) * D;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int i = lane + 32 * j;
+      if (i < 2 * kRowChunks) {
+        const int kv = i >= kRowChunks ? 1 : 0;
+        const int c = i - kv * kRowChunks;
+        const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + tok * 128 + (((c & 7) ^ (tok & 7)) << 4)
+                             : tok * D * (int)sizeof(T) + c * 16;
+        *reinterpret_cast<uint4*>(kt + kv * kTile + off) = v[j];
+        if (owner)
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? a.v_cache_w : a.k_cache_w) + dst + c * kVec) = v[j];
+      }
+    }
+    fence_proxy_async_smem();  // a later TMA write of this tile follows these stores
+    __syncwarp();
   }
-  fence_proxy_async_smem();  // a later TMA write of this tile follows these stores
-  __syncwarp();
-}
+};
 
 // ---------------------------------------------------------------------------
 // Kernel configuration (per element type / head dim).
@@ -486,6 +513,14 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
   const int span = pb1 - pb0;
   const int nb = span > warp ? (span - warp + NW - 1) / NW : 0;
   const int32_t* table = a.block_tables + (size_t)seq * a.max_blocks_per_seq + pb0 + warp;
+  AppendRow<T, D> app;
+  bool app_mine = false;
+  if constexpr (kAppend) {
+    if (last_blk >= pb0 && last_blk < pb1 && (last_blk - pb0) % NW == warp) {
+      app.load(a, seq, kvh, last_blk, ctx, lane);
+      app_mine = true;
+    }
+  }
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k_cache);
   const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v_cache);
 
@@ -552,7 +587,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     if (flags[s]) {
       uint8_t* kt = tiles + (size_t)s * 2 * TILE;
       if constexpr (kAppend) {
-        if (blk == last_blk) append_token<T, D, kMma>(a, kt, seq, kvh, blk, ctx, chunk == 0, lane);
+        if (app_mine && blk == last_blk) app.template patch<kMma>(a, kt, kvh, chunk == 0, lane);
       }
       cons.block(kt, kt + TILE, ntok, pbuf, lane);
     }

@@ -49,7 +49,7 @@ class DecodeEngine:
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, num_heads: int,
                  max_seqs: int, max_blocks_per_seq: int, max_new_tokens: int | None = None,
                  stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2,
-                 max_chunks: int = 0):
+                 max_chunks: int = 0, fused_append: bool = False):
         self.k = key_cache
         self.v = value_cache
         self.device = key_cache.device
@@ -82,6 +82,10 @@ class DecodeEngine:
             self.tmp_out = torch.empty((max_seqs, num_heads, self.parts, self.head_dim), dtype=torch.float32,
                                        device=dev)
         self.launches_per_step = 0
+        # Decode steps whose new tokens are exactly one per row, at each row's
+        # newest position, append and attend in one launch
+        # (paged_attention_append_v1/_v2) instead of reshape_and_cache + attention.
+        self.fused_append = fused_append
 
     def h2d_bytes(self, num_seqs: int, num_new: int) -> int:
         e = self.q.element_size()
@@ -91,16 +95,28 @@ class DecodeEngine:
     def d2h_bytes(self, num_seqs: int) -> int:
         return num_seqs * self.num_heads * self.head_dim * self.q.element_size()
 
-    def _attend(self, q, out, bt, cl, num_seqs: int, max_context_len: int) -> None:
+    def _attend(self, q, out, bt, cl, num_seqs: int, max_context_len: int, new=None) -> None:
+        """new = (k_new, v_new, slot_mapping) of one token per row appends it
+        in the same launch."""
         S = num_seqs
         if max_context_len <= V1_MAX_CONTEXT:
-            ops.paged_attention_v1(out, q, self.k, self.v, bt, cl, None, max_context_len, workspace=self.workspace)
+            if new is None:
+                ops.paged_attention_v1(out, q, self.k, self.v, bt, cl, None, max_context_len,
+                                       workspace=self.workspace)
+            else:
+                ops.paged_attention_append_v1(out, q, new[0], new[1], self.k, self.v, bt, cl, new[2], None,
+                                              max_context_len, workspace=self.workspace)
             split = self.workspace is not None and ops.paged_attention_v1_workspace_size(
                 q, self.k, bt, max_context_len) > 0
             self.launches_per_step = 2 if split else 1
         else:
-            ops.paged_attention_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q, self.k, self.v,
-                                   bt, cl, None, max_context_len)
+            if new is None:
+                ops.paged_attention_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q, self.k,
+                                       self.v, bt, cl, None, max_context_len)
+            else:
+                ops.paged_attention_append_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q,
+                                              new[0], new[1], self.k, self.v, bt, cl, new[2], None,
+                                              max_context_len)
             self.launches_per_step = 2
 
     def _attend_mixed(self, b, num_seqs, max_context_len, chunks):
@@ -113,16 +129,18 @@ class DecodeEngine:
                                     b.c_ctx[:nc], b.c_start[: nc + 1], None, max_q)
         self.launches_per_step += 1
 
-    def attend(self, num_seqs: int, max_context_len: int, chunks=None) -> None:
+    def attend(self, num_seqs: int, max_context_len: int, chunks=None, new=None) -> None:
         """Attention over inputs already in self.q / self.tables / self.ctx
         (the device-resident path), output in self.out; current stream.
         chunks = (num_decode, num_chunks, max_chunk_len) runs rows past
-        num_decode as prefill chunks (self.c_tables / c_ctx / c_start)."""
+        num_decode as prefill chunks (self.c_tables / c_ctx / c_start).
+        new = (k_new, v_new, slot_mapping), one token per row at its newest
+        position, is appended to the cache in the same launch."""
         S = num_seqs
         if chunks is not None:
             self._attend_mixed(self.slots_[0], S, max_context_len, chunks)
             return
-        self._attend(self.q[:S], self.out[:S], self.tables[:S], self.ctx[:S], S, max_context_len)
+        self._attend(self.q[:S], self.out[:S], self.tables[:S], self.ctx[:S], S, max_context_len, new)
 
     def step(self, q_host, k_new_host, v_new_host, slots_host, tables_host, ctx_host, out_host,
              max_context_len: int, chunks_host=None) -> torch.cuda.Event:
@@ -137,6 +155,9 @@ class DecodeEngine:
         [C], block_tables int32 [C, max_blocks]): rows past num_decode are the
         query tokens of C prefill chunks (tables_host / ctx_host then describe
         the decode rows only).
+        With fused_append and T == S, slot s must be the slot of row s's newest
+        position (context_lens[s] - 1); a row whose slot is not is recorded as
+        CF_DEVERR_SLOT and appends nothing.
         """
         S, T = q_host.shape[0], k_new_host.shape[0]
         b = self.slots_[self.n % len(self.slots_)]
@@ -161,14 +182,17 @@ class DecodeEngine:
         self.stream.wait_event(b.h2d_done)
         if b.used:
             self.stream.wait_event(b.d2h_done)  # the slot's output was copied out
+        fused = self.fused_append and chunks_host is None and T == S
         with torch.cuda.stream(self.stream):
-            ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
+            if not fused:
+                ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
             if chunks_host is not None:
                 nd, qs, cc, _ = chunks_host
                 max_q = int((qs[1:] - qs[:-1]).max()) if cc.shape[0] else 0
                 self._attend_mixed(b, S, max_context_len, (nd, cc.shape[0], max_q))
             else:
-                self._attend(b.q[:S], b.out[:S], b.tables[:S], b.ctx[:S], S, max_context_len)
+                self._attend(b.q[:S], b.out[:S], b.tables[:S], b.ctx[:S], S, max_context_len,
+                             (b.k_new[:T], b.v_new[:T], b.slots[:T]) if fused else None)
             b.compute_done.record(self.stream)
         self.d2h.wait_event(b.compute_done)
         with torch.cuda.stream(self.d2h):

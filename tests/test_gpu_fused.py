@@ -118,7 +118,7 @@ def test_negative_and_wrong_slots_append_nothing(cflib, oracle_mod):
     rng = np.random.default_rng(3)
     q, k, v, nk, nv, tables, cl, slots = _setup(rng, "bf16", 32, 8, 128, [20, 33, 700, 64])
     bad = slots.copy()
-    bad[1] = -1                      # padding row: appends nothing
+    bad[1] = -7                      # any negative slot: the row appends nothing
     bad[2] = slots[2] + 1            # not the slot of its newest position
     dq, dk, dv, dnk, dnv = _dev("bf16", q, k, v, nk, nv)
     out = torch.empty((4, 32, 128), dtype=torch.bfloat16, device="cuda")
