@@ -26,6 +26,7 @@ CF_ERR_PLAN = 5
 CF_F32 = 0
 CF_F16 = 1
 CF_BF16 = 2
+CF_FP8_E4M3 = 3
 
 # device error bits
 CF_DEVERR_BLOCK_ID = 0x1
@@ -100,6 +101,18 @@ SIGNATURES = {
         c_int32,
         [POINTER(AttentionParams), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_int32, c_void_p],
+    ),
+    "cf_paged_attention_fp8_v1": (
+        c_int32, [POINTER(AttentionParams), c_float, c_float, c_void_p, c_size_t, c_void_p],
+    ),
+    "cf_paged_attention_fp8_v2": (
+        c_int32,
+        [POINTER(AttentionParams), c_float, c_float, c_void_p, c_void_p, c_void_p, c_int32, c_void_p],
+    ),
+    "cf_reshape_and_cache_fp8": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int64,
+         c_int32, c_float, c_float, c_void_p],
     ),
     "cf_build_decode_inputs": (
         c_int32,

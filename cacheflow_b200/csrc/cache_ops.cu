@@ -55,6 +55,53 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
+// reshape_and_cache into fp8 (e4m3) caches: the same scatter, quantizing on
+// the way -- cache = e4m3(x / scale), x / scale correctly rounded in f32,
+// then rounded to nearest even with saturation to +-448.  One thread per 16
+// elements (16 output bytes) of a (token, kv head) row.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256)
+    reshape_and_cache_fp8_kernel(const T* __restrict__ key, const T* __restrict__ value,
+                                 uint8_t* __restrict__ key_cache, uint8_t* __restrict__ value_cache,
+                                 const int32_t* __restrict__ slot_mapping, int64_t num_rows,
+                                 int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                 int64_t num_slots, float k_scale, float v_scale) {
+  const int32_t vpr = head_dim / 16;
+  const int64_t total = num_rows * vpr;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = g / vpr;
+    const int32_t v = (int32_t)(g - row * vpr);
+    const int64_t tok = row / num_kv_heads;
+    const int32_t head = (int32_t)(row - tok * num_kv_heads);
+    const int64_t slot = slot_mapping[tok];
+    if (slot < 0) continue;  // padding token
+    if (slot >= num_slots) {
+      if (v == 0) cache_error(CF_DEVERR_SLOT);
+      continue;
+    }
+    const int64_t blk = slot / block_size;
+    const int64_t off = slot - blk * block_size;
+    const int64_t dst = ((blk * num_kv_heads + head) * block_size + off) * head_dim + v * 16;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const float sc = kv ? v_scale : k_scale;
+      float f[16];
+      load_widen<T, 16>((kv ? value : key) + row * head_dim + v * 16, f);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = f2_to_e4m3x2(__fdiv_rn(f[4 * i], sc), __fdiv_rn(f[4 * i + 1], sc));
+        const uint32_t hi = f2_to_e4m3x2(__fdiv_rn(f[4 * i + 2], sc), __fdiv_rn(f[4 * i + 3], sc));
+        w[i] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>((kv ? value_cache : key_cache) + dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Block-pair copy.  Up to two (src base, dst base) streams share one list of
 // (src id, dst id) pairs: copy_blocks uses (K,K) and (V,V) within one pool,
 // swap_blocks uses one (src pool, dst pool) stream, compact uses (K,K),(V,V)
@@ -235,6 +282,40 @@ cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t
   PairIds<int32_t> ids{src_ids, dst_ids, 1};
   return launch_pairs<int32_t, true>(st, ids, num_moves, block_bytes, num_blocks, num_blocks,
                                      stream);
+}
+
+cf_status launch_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
+                                       void* value_cache, const int32_t* slot_mapping,
+                                       int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t block_size, int64_t num_blocks, int32_t dtype,
+                                       float k_scale, float v_scale, cudaStream_t stream) {
+  if (num_tokens == 0) return CF_OK;
+  const int64_t rows = (int64_t)num_tokens * num_kv_heads;
+  const int64_t total = rows * (head_dim / 16);
+  const int64_t want = (total + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const int64_t slots = num_blocks * block_size;
+  uint8_t* kc = static_cast<uint8_t*>(key_cache);
+  uint8_t* vc = static_cast<uint8_t*>(value_cache);
+  switch (dtype) {
+    case CF_F32:
+      reshape_and_cache_fp8_kernel<float><<<grid, 256, 0, stream>>>(
+          (const float*)key, (const float*)value, kc, vc, slot_mapping, rows, num_kv_heads, head_dim,
+          block_size, slots, k_scale, v_scale);
+      break;
+    case CF_F16:
+      reshape_and_cache_fp8_kernel<__half><<<grid, 256, 0, stream>>>(
+          (const __half*)key, (const __half*)value, kc, vc, slot_mapping, rows, num_kv_heads, head_dim,
+          block_size, slots, k_scale, v_scale);
+      break;
+    default:
+      reshape_and_cache_fp8_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+          (const __nv_bfloat16*)key, (const __nv_bfloat16*)value, kc, vc, slot_mapping, rows,
+          num_kv_heads, head_dim, block_size, slots, k_scale, v_scale);
+      break;
+  }
+  return check_launch();
 }
 
 cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_listed,

@@ -4,6 +4,7 @@
 // dispatch to the launchers, status / error-word plumbing, the copy-engine
 // swap path and the host-side compaction planner.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -103,15 +104,33 @@ cf_status check_attention_params(const cf_paged_attention_params* p, bool check_
 
 size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out);
 
-// cf_paged_attention_v1 / _append_v1 (key == nullptr: no append).
+// Launch extras beyond the attention params: the fused append's rows and an
+// fp8 cache's element type and scales.
+struct Extras {
+  const void* key = nullptr;
+  const void* value = nullptr;
+  const int32_t* slots = nullptr;
+  int32_t cache_dtype = -1;
+  float k_scale = 1.f;
+  float v_scale = 1.f;
+};
+
+void apply(AttnLaunch& l, const Extras& x) {
+  l.new_k = x.key;
+  l.new_v = x.value;
+  l.slot_mapping = x.slots;
+  l.cache_dtype = x.cache_dtype;
+  l.k_scale = x.k_scale;
+  l.v_scale = x.v_scale;
+}
+
+// cf_paged_attention_v1 and its append / fp8 forms.
 cf_status run_v1(const cf_paged_attention_params* p, void* workspace, size_t workspace_bytes,
-                 void* stream, const void* key, const void* value, const int32_t* slots) {
+                 void* stream, const Extras& x) {
   cf_status st = check_attention_params(p);
   if (st != CF_OK || p->num_seqs == 0) return st;
   AttnLaunch l{p, 0, 1, nullptr, nullptr, nullptr, (cudaStream_t)stream};
-  l.new_k = key;
-  l.new_v = value;
-  l.slot_mapping = slots;
+  apply(l, x);
   int32_t parts = 0;
   const size_t need = v1_split_bytes(p, &parts);
   if (need > 0 && workspace != nullptr && workspace_bytes >= need) {
@@ -128,10 +147,9 @@ cf_status run_v1(const cf_paged_attention_params* p, void* workspace, size_t wor
   return launch_paged_attention(l);
 }
 
-// cf_paged_attention_v2 / _append_v2.
+// cf_paged_attention_v2 and its append / fp8 forms.
 cf_status run_v2(const cf_paged_attention_params* p, float* exp_sums, float* max_logits,
-                 float* tmp_output, int32_t num_partitions, void* stream, const void* key,
-                 const void* value, const int32_t* slots) {
+                 float* tmp_output, int32_t num_partitions, void* stream, const Extras& x) {
   cf_status st = check_attention_params(p);
   if (st != CF_OK || p->num_seqs == 0) return st;
   if (!exp_sums || !max_logits || !tmp_output || num_partitions < 1)
@@ -140,10 +158,27 @@ cf_status run_v2(const cf_paged_attention_params* p, float* exp_sums, float* max
   if (need > num_partitions) return CF_ERR_WORKSPACE;
   AttnLaunch l{p, kV2PartitionTokens, num_partitions, max_logits, exp_sums, tmp_output,
                (cudaStream_t)stream};
-  l.new_k = key;
-  l.new_v = value;
-  l.slot_mapping = slots;
+  apply(l, x);
   return launch_paged_attention(l);
+}
+
+// Shape and scale checks of the fp8-cache entry points (params->dtype is the
+// query / output type).
+cf_status check_fp8(const cf_paged_attention_params* p, float k_scale, float v_scale) {
+  if (p == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return CF_ERR_INVALID_ARGUMENT;
+  if (p->dtype != CF_F16 && p->dtype != CF_BF16) return CF_ERR_UNSUPPORTED;
+  if (!attention_fp8_supported(p->head_dim, p->block_size, p->dtype)) return CF_ERR_UNSUPPORTED;
+  return CF_OK;
+}
+
+Extras fp8_extras(float k_scale, float v_scale) {
+  Extras x;
+  x.cache_dtype = CF_FP8_E4M3;
+  x.k_scale = k_scale;
+  x.v_scale = v_scale;
+  return x;
 }
 
 size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out) {
@@ -187,14 +222,13 @@ size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) 
 
 cf_status cf_paged_attention_v1(const cf_paged_attention_params* p, void* workspace,
                                 size_t workspace_bytes, void* stream) {
-  return run_v1(p, workspace, workspace_bytes, stream, nullptr, nullptr, nullptr);
+  return run_v1(p, workspace, workspace_bytes, stream, Extras{});
 }
 
 cf_status cf_paged_attention_v2(const cf_paged_attention_params* p, float* exp_sums,
                                 float* max_logits, float* tmp_output, int32_t num_partitions,
                                 void* stream) {
-  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, nullptr, nullptr,
-                nullptr);
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, Extras{});
 }
 
 cf_status cf_paged_attention_append_v1(const cf_paged_attention_params* p, const void* key,
@@ -203,7 +237,11 @@ cf_status cf_paged_attention_append_v1(const cf_paged_attention_params* p, const
   // The append writes the caches: block ids must be range-checked (num_blocks > 0).
   if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
   if (p && p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
-  return run_v1(p, workspace, workspace_bytes, stream, key, value, slot_mapping);
+  Extras x;
+  x.key = key;
+  x.value = value;
+  x.slots = slot_mapping;
+  return run_v1(p, workspace, workspace_bytes, stream, x);
 }
 
 cf_status cf_paged_attention_append_v2(const cf_paged_attention_params* p, const void* key,
@@ -212,8 +250,49 @@ cf_status cf_paged_attention_append_v2(const cf_paged_attention_params* p, const
                                        int32_t num_partitions, void* stream) {
   if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
   if (p && p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
-  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, key, value,
-                slot_mapping);
+  Extras x;
+  x.key = key;
+  x.value = value;
+  x.slots = slot_mapping;
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, x);
+}
+
+cf_status cf_paged_attention_fp8_v1(const cf_paged_attention_params* p, float k_scale,
+                                    float v_scale, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  const cf_status st = check_fp8(p, k_scale, v_scale);
+  if (st != CF_OK) return st;
+  return run_v1(p, workspace, workspace_bytes, stream, fp8_extras(k_scale, v_scale));
+}
+
+cf_status cf_paged_attention_fp8_v2(const cf_paged_attention_params* p, float k_scale,
+                                    float v_scale, float* exp_sums, float* max_logits,
+                                    float* tmp_output, int32_t num_partitions, void* stream) {
+  const cf_status st = check_fp8(p, k_scale, v_scale);
+  if (st != CF_OK) return st;
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream,
+                fp8_extras(k_scale, v_scale));
+}
+
+cf_status cf_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
+                                   void* value_cache, const int32_t* slot_mapping,
+                                   int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                   int32_t block_size, int64_t num_blocks, int32_t dtype,
+                                   float k_scale, float v_scale, void* stream) {
+  if ((dtype != CF_F32 && dtype != CF_F16 && dtype != CF_BF16) || num_tokens < 0 ||
+      num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return CF_ERR_INVALID_ARGUMENT;
+  if (head_dim % 16 != 0) return CF_ERR_UNSUPPORTED;
+  if (num_tokens == 0) return CF_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping) return CF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(key) || !aligned16(value) || !aligned16(key_cache) || !aligned16(value_cache))
+    return CF_ERR_INVALID_ARGUMENT;
+  const int64_t nb = num_blocks > 0 ? num_blocks : INT64_MAX / ((int64_t)block_size * 2);
+  return launch_reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping,
+                                      num_tokens, num_kv_heads, head_dim, block_size, nb, dtype,
+                                      k_scale, v_scale, (cudaStream_t)stream);
 }
 
 cf_status cf_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,

@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -14,8 +15,8 @@
 namespace cfb {
 
 // ---------------------------------------------------------------------------
-// Element types.  Caches hold float, __half or __nv_bfloat16; all arithmetic
-// is float32.
+// Element types.  Caches hold float, __half, __nv_bfloat16 or (caches only)
+// __nv_fp8_e4m3 scaled by a per-cache factor; all arithmetic is float32.
 // ---------------------------------------------------------------------------
 template <typename T>
 struct ElemTraits;
@@ -31,6 +32,22 @@ template <>
 struct ElemTraits<__nv_bfloat16> {
   static constexpr cf_dtype kDtype = CF_BF16;
 };
+template <>
+struct ElemTraits<__nv_fp8_e4m3> {
+  static constexpr cf_dtype kDtype = CF_FP8_E4M3;
+};
+
+// Two e4m3 values (low byte first) -> f16x2 (low half first); exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(two & 0xffffu), __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+// Two floats -> two e4m3 (low byte first): round to nearest even, values
+// beyond the largest finite (448) saturate to it.
+__device__ __forceinline__ uint16_t f2_to_e4m3x2(float x, float y) {
+  return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(x, y), __NV_SATFINITE, __NV_E4M3);
+}
 
 // Unpack one 32-bit word of packed elements into floats.
 template <typename T>
@@ -51,6 +68,17 @@ __device__ __forceinline__ void unpack_word<__half>(uint32_t w, float* f) {
   float2 v = __half22float2(h);
   f[0] = v.x;
   f[1] = v.y;
+}
+
+template <>
+__device__ __forceinline__ void unpack_word<__nv_fp8_e4m3>(uint32_t w, float* f) {
+  const uint32_t lo = e4m3x2_to_h2(w), hi = e4m3x2_to_h2(w >> 16);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
 }
 
 template <typename T>

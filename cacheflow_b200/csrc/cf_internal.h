@@ -17,7 +17,7 @@ cf_status cuda_status(cudaError_t err);
 inline cf_status check_launch() { return cuda_status(cudaGetLastError()); }
 
 inline int dtype_bytes(int32_t dtype) {
-  return dtype == CF_F32 ? 4 : (dtype == CF_F16 || dtype == CF_BF16) ? 2 : 0;
+  return dtype == CF_F32 ? 4 : (dtype == CF_F16 || dtype == CF_BF16) ? 2 : dtype == CF_FP8_E4M3 ? 1 : 0;
 }
 
 inline bool aligned16(const void* p) {
@@ -37,11 +37,19 @@ struct AttnLaunch {
   const void* new_k = nullptr;  // [num_seqs, num_kv_heads, head_dim]
   const void* new_v = nullptr;
   const int32_t* slot_mapping = nullptr;  // [num_seqs] or null
+  // Element type of the caches when it differs from p->dtype (CF_FP8_E4M3),
+  // else -1; an fp8 cache holds K / k_scale and V / v_scale.
+  int32_t cache_dtype = -1;
+  float k_scale = 1.f;
+  float v_scale = 1.f;
 };
 cf_status launch_paged_attention(const AttnLaunch& l);
 bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype);
-// K or V cache as a 2-D tensor map [rows, D] of 16-bit elements, boxes of
-// 16 rows x 64 elements with the 128-byte swizzle; false if it cannot be encoded.
+// fp8 (e4m3) caches with f16 / bf16 queries.
+bool attention_fp8_supported(int32_t head_dim, int32_t block_size, int32_t dtype);
+// K or V cache as a 2-D tensor map [rows, D] of 16-bit (or fp8) elements,
+// boxes of 16 rows x 128 bytes (64 or 128 elements) with the 128-byte
+// swizzle; false if it cannot be encoded.
 bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int32_t dtype);
 cf_status attention_read_errors(uint32_t* bits, bool clear);
 
@@ -70,6 +78,12 @@ cf_status launch_build_decode_inputs(const int32_t* positions, const int64_t* bl
                                      int32_t max_blocks_per_seq, int32_t block_size,
                                      int32_t* block_tables, int32_t* context_lens,
                                      int32_t* slot_mapping, cudaStream_t stream);
+// Quantizing scatter into fp8 (e4m3) caches: cache = e4m3(kv / scale).
+cf_status launch_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
+                                       void* value_cache, const int32_t* slot_mapping,
+                                       int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t block_size, int64_t num_blocks, int32_t dtype,
+                                       float k_scale, float v_scale, cudaStream_t stream);
 cf_status cache_ops_read_errors(uint32_t* bits, bool clear);
 
 }  // namespace cfb

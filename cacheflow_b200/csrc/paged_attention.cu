@@ -77,6 +77,7 @@ struct AttnArgs {
   const int32_t* slot_mapping;  // [S] or null (slot from the block table)
   void* k_cache_w;              // the caches, written by the append
   void* v_cache_w;
+  float v_scale;                // fp8 caches: V = stored * v_scale (else 1)
 };
 
 // ---------------------------------------------------------------------------
@@ -85,10 +86,10 @@ struct AttnArgs {
 // shared-memory reads are conflict-free without swizzling), PV with lane l
 // owning columns [l*D/32, (l+1)*D/32).
 // ---------------------------------------------------------------------------
-template <typename T, int D, int HG>
+template <typename T, typename TC, int D, int HG>
 struct FmaConsumer {
-  static constexpr int kVec = 16 / (int)sizeof(T);           // elements per 16 B
-  static constexpr int kChunks = D * (int)sizeof(T) / 128;   // 16 B chunks per lane (QK)
+  static constexpr int kVec = 16 / (int)sizeof(TC);          // cache elements per 16 B
+  static constexpr int kChunks = D * (int)sizeof(TC) / 128;  // 16 B chunks per lane (QK)
   static constexpr int kEpl = D / 32;                        // columns per lane (PV)
   static_assert(kChunks >= 1, "head_dim too small for this element type");
 
@@ -119,9 +120,9 @@ struct FmaConsumer {
     }
   }
 
-  __device__ __forceinline__ void pv_token(const T* vrow, const float* pt_h, int t) {
+  __device__ __forceinline__ void pv_token(const TC* vrow, const float* pt_h, int t) {
     float vf[kEpl];
-    load_widen<T, kEpl>(vrow + t * D, vf);
+    load_widen<TC, kEpl>(vrow + t * D, vf);
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
       const float pt = pt_h[h * kBlockTokens + t];
@@ -134,22 +135,22 @@ struct FmaConsumer {
   // HG*16-float scratch.
   __device__ __forceinline__ void block(const uint8_t* kraw, const uint8_t* vraw, int ntok,
                                         float* pbuf, int lane) {
-    const T* kt = reinterpret_cast<const T*>(kraw);
-    const T* vt = reinterpret_cast<const T*>(vraw);
+    const TC* kt = reinterpret_cast<const TC*>(kraw);
+    const TC* vt = reinterpret_cast<const TC*>(vraw);
     const int j = lane >> 3;
     const int i = lane & 7;
     float s[4][HG];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const int tok = p * 4 + j;
-      const T* row = kt + tok * D;
+      const TC* row = kt + tok * D;
       float acc[HG];
 #pragma unroll
       for (int h = 0; h < HG; ++h) acc[h] = 0.f;
 #pragma unroll
       for (int k = 0; k < kChunks; ++k) {
         float kf[kVec];
-        load_widen<T, kVec>(row + (i + 8 * k) * kVec, kf);
+        load_widen<TC, kVec>(row + (i + 8 * k) * kVec, kf);
 #pragma unroll
         for (int h = 0; h < HG; ++h)
 #pragma unroll
@@ -190,7 +191,7 @@ struct FmaConsumer {
       }
     }
     __syncwarp();
-    const T* vrow = vt + lane * kEpl;
+    const TC* vrow = vt + lane * kEpl;
     if (ntok == kBlockTokens) {
 #pragma unroll
       for (int t = 0; t < kBlockTokens; ++t) pv_token(vrow, pbuf, t);
@@ -363,6 +364,174 @@ struct MmaConsumer {
 };
 
 // ---------------------------------------------------------------------------
+// Tensor-core consumer for fp8 (e4m3) caches with f16 / bf16 queries.  The
+// MMAs run in f16 (e4m3 -> f16 is exact; queries are rounded to f16, exact
+// for bf16 values of magnitude 2^-14 .. 65504).  Tiles arrive as for the
+// 16-bit consumer: 16 rows x 128-byte boxes (128 e4m3 per box row) with the
+// 128-byte swizzle.  No transposing load exists for bytes, so both products
+// reorder a contracted or output dimension instead:
+//   S = Q.K^T: ldmatrix (b16 view) hands thread (g, t) bytes 4t..4t+3 of a
+//     16-byte chunk of token row g; the low two feed k-slots 2t, 2t+1 and the
+//     high two k-slots 2t+8, 2t+9.  Q's A fragment is loaded with the same
+//     order (elements 4t..4t+3 of the chunk), so the dot product is unchanged.
+//   O += P.V: ldmatrix.trans (b16 view) hands thread (g, t) the byte pairs
+//     (2g, 2g+1) of tokens 2t and 2t+1; a byte permute pairs the even column
+//     of both tokens and the odd column of both tokens, giving the B
+//     fragments of two n-tiles: one over the chunk's even columns, one over
+//     its odd columns.  store() writes each accumulator column back to its
+//     true position.
+// P is split into an f16 head and remainder (rows g / g+8) as in the 16-bit
+// consumer.  The per-cache scales are applied outside: k_scale is folded into
+// the logit scale, v_scale into the final output.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+struct MmaConsumerFp8 {
+  static_assert(D % 128 == 0, "fp8 tiles are whole 128-byte boxes");
+  static constexpr int kKC = D / 16;   // k-steps of QK = 16-byte chunks of a row
+  static constexpr int kND = D / 8;    // n-tiles of PV (each chunk: even and odd columns)
+  static constexpr int kBoxBytes = kBlockTokens * 128;
+
+  uint32_t qa[kKC][2];
+  float o[kND][4];
+  float m;
+  float l;
+  float scale_log2;
+
+  __device__ __forceinline__ void init(const T* qrow, int nheads, float sl2, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int kc = 0; kc < kKC; ++kc) {
+      if (g < nheads) {
+        float f[4];
+        load_widen<T, 4>(qrow + (size_t)g * D + kc * 16 + 4 * t, f);
+        qa[kc][0] = pack2<__half>(f[0], f[1]);
+        qa[kc][1] = pack2<__half>(f[2], f[3]);
+      } else {
+        qa[kc][0] = qa[kc][1] = 0u;
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < kND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    m = -INFINITY;
+    l = 0.f;
+    scale_log2 = sl2;
+  }
+
+  __device__ __forceinline__ void block(const uint8_t* kt, const uint8_t* vt, int ntok, float*,
+                                        int lane) {
+    const int t = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
+    const uint32_t kbase = smem_addr(kt), vbase = smem_addr(vt);
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      // matrix mi: tokens (mi >> 1) * 8 .., chunk kc + (mi & 1)
+      const int r = (mi >> 1) * 8 + ri;
+      const uint32_t rowa = kbase + r * 128;
+#pragma unroll
+      for (int kc = 0; kc < kKC; kc += 2) {
+        const int c = kc + (mi & 1);
+        uint32_t x0, x1, x2, x3;
+        ldmatrix_x4(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), x0, x1, x2, x3);
+        mma_16816<__half>(s[0], qa[kc][0], 0u, qa[kc][1], 0u, e4m3x2_to_h2(x0), e4m3x2_to_h2(x0 >> 16));
+        mma_16816<__half>(s[1], qa[kc][0], 0u, qa[kc][1], 0u, e4m3x2_to_h2(x2), e4m3x2_to_h2(x2 >> 16));
+        mma_16816<__half>(s[0], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, e4m3x2_to_h2(x1),
+                          e4m3x2_to_h2(x1 >> 16));
+        mma_16816<__half>(s[1], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, e4m3x2_to_h2(x3),
+                          e4m3x2_to_h2(x3 >> 16));
+      }
+    }
+    float bm = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int tok = nt * 8 + 2 * t + j;
+        const float x = s[nt][j] * scale_log2;
+        s[nt][j] = tok < ntok ? x : -INFINITY;
+        bm = fmaxf(bm, s[nt][j]);
+      }
+    bm = fmaxf(bm, shfl_xor(bm, 1));
+    bm = fmaxf(bm, shfl_xor(bm, 2));
+    const float mn = fmaxf(m, bm);
+    const float mu = (mn == -INFINITY) ? 0.f : mn;
+    const float alpha = exp2f(m - mu);
+    m = mn;
+    float ps = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        s[nt][j] = exp2f(s[nt][j] - mu);
+        ps += s[nt][j];
+      }
+    l = l * alpha + ps;
+#pragma unroll
+    for (int n = 0; n < kND; ++n) {
+      o[n][0] *= alpha;
+      o[n][1] *= alpha;
+      o[n][2] *= alpha;
+      o[n][3] *= alpha;
+    }
+    uint32_t pa[4];
+    split2<__half>(s[0][0], s[0][1], pa[0], pa[1]);
+    split2<__half>(s[1][0], s[1][1], pa[2], pa[3]);
+
+    if (ntok < kBlockTokens) {
+      // Rows past the context may hold NaN patterns; 0 * NaN is not 0.
+      constexpr int kChunksPerRow = D / 16;
+      const int n = (kBlockTokens - ntok) * kChunksPerRow;
+      for (int i = lane; i < n; i += 32) {
+        const int r = ntok + i / kChunksPerRow;
+        const int c = i % kChunksPerRow;
+        *reinterpret_cast<uint4*>(const_cast<uint8_t*>(vt) + (c >> 3) * kBoxBytes + r * 128 +
+                                  ((c & 7) << 4)) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+    {
+      // matrix mi: tokens (mi & 1) * 8 .., chunk 2 * cp + (mi >> 1)
+      const int r = (mi & 1) * 8 + ri;
+      const uint32_t rowa = vbase + r * 128;
+#pragma unroll
+      for (int cp = 0; cp < kKC / 2; ++cp) {
+        const int c = 2 * cp + (mi >> 1);
+        uint32_t y0, y1, y2, y3;
+        ldmatrix_x4_trans(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), y0, y1, y2, y3);
+        // chunk 2cp: tokens 0-7 in y0, 8-15 in y1; chunk 2cp+1: y2, y3.
+        mma_16816<__half>(o[4 * cp + 0], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y0, 0, 0x20)),
+                          e4m3x2_to_h2(__byte_perm(y1, 0, 0x20)));
+        mma_16816<__half>(o[4 * cp + 1], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y0, 0, 0x31)),
+                          e4m3x2_to_h2(__byte_perm(y1, 0, 0x31)));
+        mma_16816<__half>(o[4 * cp + 2], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y2, 0, 0x20)),
+                          e4m3x2_to_h2(__byte_perm(y3, 0, 0x20)));
+        mma_16816<__half>(o[4 * cp + 3], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y2, 0, 0x31)),
+                          e4m3x2_to_h2(__byte_perm(y3, 0, 0x31)));
+      }
+    }
+  }
+
+  // n-tile 2c + p (p = 0 even, 1 odd columns of chunk c): accumulator column
+  // j of the tile is head dimension 16c + 2j + p.
+  __device__ __forceinline__ void store(float* mo, float* mm, float* ml, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int n = 0; n < kND; ++n) {
+      const int d = (n >> 1) * 16 + 4 * t + (n & 1);
+      mo[g * D + d] = o[n][0] + o[n][2];
+      mo[g * D + d + 2] = o[n][1] + o[n][3];
+    }
+    float lt = l;
+    lt += shfl_xor(lt, 1);
+    lt += shfl_xor(lt, 2);
+    if (t == 0) {
+      mm[g] = m;
+      ml[g] = lt;
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
 // Fused append: the warp that will hold block `blk` (the one with the row's
 // newest token) loads the new K/V row, the block id and the slot before its
 // pipeline starts (so the patch waits on nothing); when that block's tile
@@ -454,13 +623,17 @@ struct AttnConfig {
   static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
 };
 
-template <typename T, int D, int HG, bool kMma, bool kAppend>
-__global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
+template <typename T, typename TC, int D, int HG, bool kMma, bool kAppend>
+__global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32)
     paged_attention_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv) {
-  using Cfg = AttnConfig<T, D, HG>;
-  using Consumer = std::conditional_t<kMma, MmaConsumer<T, D>, FmaConsumer<T, D, HG>>;
+  // T: query / output type; TC: cache type (T, or fp8 e4m3 with T 16-bit).
+  using Cfg = AttnConfig<TC, D, HG>;
+  constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+  using Consumer = std::conditional_t<kMma, std::conditional_t<kFp8, MmaConsumerFp8<T, D>, MmaConsumer<T, D>>,
+                                      FmaConsumer<T, TC, D, HG>>;
   static_assert(!kMma || HG == 8, "the tensor-core consumer covers 8 query heads");
+  static_assert(!kAppend || std::is_same<T, TC>::value, "the fused append writes caches of the query type");
   constexpr int NW = Cfg::kWarps;
   constexpr int S = Cfg::kStages;
   constexpr int TILE = Cfg::kTileBytes;
@@ -542,13 +715,14 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
     mbar_arrive_expect_tx(bar, 2 * TILE);
     uint8_t* kt = tiles + (size_t)s * 2 * TILE;
     if constexpr (kMma) {
-      // Boxes of 16 rows x 64 elements (128 bytes, swizzled); x stays a
-      // multiple of 64 elements.
+      // Boxes of 16 rows x 128 bytes (64 16-bit or 128 fp8 elements,
+      // swizzled); x stays a multiple of the box width.
+      constexpr int kBoxElems = 128 / (int)sizeof(TC);
       const int32_t row = (int32_t)(((int64_t)phys * a.num_kv_heads + kvh) * kBlockTokens);
 #pragma unroll
-      for (int b = 0; b < D / 64; ++b) {
-        tma_load_2d(smem_addr(kt + b * kBlockTokens * 128), &tmk, b * 64, row, bar);
-        tma_load_2d(smem_addr(kt + TILE + b * kBlockTokens * 128), &tmv, b * 64, row, bar);
+      for (int b = 0; b < D / kBoxElems; ++b) {
+        tma_load_2d(smem_addr(kt + b * kBlockTokens * 128), &tmk, b * kBoxElems, row, bar);
+        tma_load_2d(smem_addr(kt + TILE + b * kBlockTokens * 128), &tmv, b * kBoxElems, row, bar);
       }
     } else {
       const size_t off = ((size_t)phys * a.num_kv_heads + kvh) * (size_t)TILE;
@@ -627,7 +801,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, HG>::kWarps * 32)
         acc = fmaf(mo[(w * HG + h) * D + d], sc, acc);
       }
     }
-    const float res = L > 0.f ? acc / L : 0.f;
+    const float res = L > 0.f ? acc / L * a.v_scale : 0.f;
     const size_t hq = (size_t)seq * H + head0 + h;
     if (single) {
       reinterpret_cast<T*>(a.out)[hq * D + d] = from_float<T>(res);
@@ -773,12 +947,15 @@ static EncodeTiledFn encode_tiled() {
 bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int32_t dtype) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return false;
+  const int eb = dtype == CF_FP8_E4M3 ? 1 : 2;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)kBlockTokens};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * eb};
+  const cuuint32_t box[2] = {(cuuint32_t)(128 / eb), (cuuint32_t)kBlockTokens};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, dtype == CF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void*>(base), dims, strides, box, estr,
+  const CUtensorMapDataType ty = dtype == CF_FP8_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dtype == CF_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, ty, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -787,11 +964,11 @@ bool kv_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int D, int3
 namespace {
 
 // Per kernel instantiation and device: opt in to > 48 KB of dynamic smem.
-template <typename T, int D, int HG, bool kMma, bool kAppend>
+template <typename T, typename TC, int D, int HG, bool kMma, bool kAppend>
 cf_status ensure_smem(int bytes) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
-  auto kern = paged_attention_kernel<T, D, HG, kMma, kAppend>;
+  auto kern = paged_attention_kernel<T, TC, D, HG, kMma, kAppend>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -807,15 +984,15 @@ struct Maps {
   CUtensorMap k, v;
 };
 
-template <typename T, int D, int HG, bool kMma, bool kAppend>
+template <typename T, typename TC, int D, int HG, bool kMma, bool kAppend>
 cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& maps) {
-  using Cfg = AttnConfig<T, D, HG>;
+  using Cfg = AttnConfig<TC, D, HG>;
   const cf_paged_attention_params& p = *l.p;
   a.head_chunks = (a.group + HG - 1) / HG;
-  cf_status st = ensure_smem<T, D, HG, kMma, kAppend>(Cfg::kSmemAlloc);
+  cf_status st = ensure_smem<T, TC, D, HG, kMma, kAppend>(Cfg::kSmemAlloc);
   if (st != CF_OK) return st;
   dim3 grid((unsigned)grid_x, (unsigned)(p.num_kv_heads * a.head_chunks), (unsigned)p.num_seqs);
-  paged_attention_kernel<T, D, HG, kMma, kAppend>
+  paged_attention_kernel<T, TC, D, HG, kMma, kAppend>
       <<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a, maps.k, maps.v);
   st = check_launch();
   if (st != CF_OK || l.part_max == nullptr || grid_x == 1) return st;
@@ -848,9 +1025,11 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
 }
 
 // Which consumer runs: tensor cores for GQA groups of 3+ query heads on 16-bit
-// caches, FMA otherwise.  CF_ATTN_CONSUMER=fma|mma overrides (read per call).
-bool use_mma(const cf_paged_attention_params& p, int64_t rows) {
-  if (p.dtype == CF_F32 || p.num_blocks <= 0 || rows > INT32_MAX || p.head_dim % 64 != 0) return false;
+// caches (fp8 caches: head_dim a multiple of 128), FMA otherwise.
+// CF_ATTN_CONSUMER=fma|mma overrides (read per call).
+bool use_mma(const cf_paged_attention_params& p, int64_t rows, bool fp8) {
+  if (p.dtype == CF_F32 || p.num_blocks <= 0 || rows > INT32_MAX) return false;
+  if (p.head_dim % (fp8 ? 128 : 64) != 0) return false;
   if (const char* e = std::getenv("CF_ATTN_CONSUMER")) {
     if (std::strcmp(e, "fma") == 0) return false;
     if (std::strcmp(e, "mma") == 0) return true;
@@ -858,38 +1037,55 @@ bool use_mma(const cf_paged_attention_params& p, int64_t rows) {
   return p.num_heads / p.num_kv_heads >= 3;
 }
 
-template <typename T, int D, bool kAppend>
+template <typename T, typename TC, int D, bool kAppend>
 cf_status launch_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
+  constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
   const cf_paged_attention_params& p = *l.p;
   Maps maps;
   std::memset(&maps, 0, sizeof(maps));
-  if constexpr (sizeof(T) == 2) {
+  if constexpr (sizeof(T) == 2 && (!kFp8 || D % 128 == 0)) {
+    const int32_t cdt = kFp8 ? (int32_t)CF_FP8_E4M3 : p.dtype;
     const int64_t rows = p.num_blocks * (int64_t)p.num_kv_heads * kBlockTokens;
-    if (use_mma(p, rows) && kv_tensor_map(&maps.k, p.key_cache, rows, D, p.dtype) &&
-        kv_tensor_map(&maps.v, p.value_cache, rows, D, p.dtype))
-      return launch_typed<T, D, 8, true, kAppend>(l, a, grid_x, maps);
+    if (use_mma(p, rows, kFp8) && kv_tensor_map(&maps.k, p.key_cache, rows, D, cdt) &&
+        kv_tensor_map(&maps.v, p.value_cache, rows, D, cdt))
+      return launch_typed<T, TC, D, 8, true, kAppend>(l, a, grid_x, maps);
   }
-  if (a.group == 1) return launch_typed<T, D, 1, false, kAppend>(l, a, grid_x, maps);
-  if (a.group == 2) return launch_typed<T, D, 2, false, kAppend>(l, a, grid_x, maps);
-  return launch_typed<T, D, 4, false, kAppend>(l, a, grid_x, maps);
+  if (a.group == 1) return launch_typed<T, TC, D, 1, false, kAppend>(l, a, grid_x, maps);
+  if (a.group == 2) return launch_typed<T, TC, D, 2, false, kAppend>(l, a, grid_x, maps);
+  return launch_typed<T, TC, D, 4, false, kAppend>(l, a, grid_x, maps);
 }
 
-template <typename T, bool kAppend>
+template <typename T, typename TC, bool kAppend>
 cf_status launch_head_dim(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
-  switch (l.p->head_dim) {
-    case 64: return launch_dim<T, 64, kAppend>(l, a, grid_x);
-    case 128: return launch_dim<T, 128, kAppend>(l, a, grid_x);
-    case 256:
-      if constexpr (sizeof(T) == 2) return launch_dim<T, 256, kAppend>(l, a, grid_x);
-      return CF_ERR_UNSUPPORTED;
-    default: return CF_ERR_UNSUPPORTED;
+  if constexpr (std::is_same<TC, __nv_fp8_e4m3>::value) {
+    switch (l.p->head_dim) {
+      case 128: return launch_dim<T, TC, 128, kAppend>(l, a, grid_x);
+      case 256: return launch_dim<T, TC, 256, kAppend>(l, a, grid_x);
+      default: return CF_ERR_UNSUPPORTED;
+    }
+  } else {
+    switch (l.p->head_dim) {
+      case 64: return launch_dim<T, TC, 64, kAppend>(l, a, grid_x);
+      case 128: return launch_dim<T, TC, 128, kAppend>(l, a, grid_x);
+      case 256:
+        if constexpr (sizeof(T) == 2) return launch_dim<T, TC, 256, kAppend>(l, a, grid_x);
+        return CF_ERR_UNSUPPORTED;
+      default: return CF_ERR_UNSUPPORTED;
+    }
   }
 }
 
 template <typename T>
 cf_status launch_type(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
-  return a.new_k != nullptr ? launch_head_dim<T, true>(l, a, grid_x)
-                            : launch_head_dim<T, false>(l, a, grid_x);
+  if (l.cache_dtype == CF_FP8_E4M3) {
+    if constexpr (sizeof(T) == 2) {
+      if (a.new_k != nullptr) return CF_ERR_UNSUPPORTED;
+      return launch_head_dim<T, __nv_fp8_e4m3, false>(l, a, grid_x);
+    }
+    return CF_ERR_UNSUPPORTED;
+  }
+  return a.new_k != nullptr ? launch_head_dim<T, T, true>(l, a, grid_x)
+                            : launch_head_dim<T, T, false>(l, a, grid_x);
 }
 
 }  // namespace
@@ -900,6 +1096,11 @@ bool attention_supported(int32_t head_dim, int32_t block_size, int32_t dtype) {
   if (dtype == CF_F16 || dtype == CF_BF16)
     return head_dim == 64 || head_dim == 128 || head_dim == 256;
   return false;
+}
+
+bool attention_fp8_supported(int32_t head_dim, int32_t block_size, int32_t dtype) {
+  return block_size == kBlockTokens && (dtype == CF_F16 || dtype == CF_BF16) &&
+         (head_dim == 128 || head_dim == 256);
 }
 
 cf_status launch_paged_attention(const AttnLaunch& l) {
@@ -915,7 +1116,8 @@ cf_status launch_paged_attention(const AttnLaunch& l) {
   a.part_max = l.part_max;
   a.part_sum = l.part_sum;
   a.part_out = l.part_out;
-  a.scale_log2 = p.scale * kLog2e;
+  a.scale_log2 = p.scale * kLog2e * l.k_scale;
+  a.v_scale = l.v_scale;
   a.num_heads = p.num_heads;
   a.num_kv_heads = p.num_kv_heads;
   a.group = p.num_heads / p.num_kv_heads;

@@ -29,6 +29,12 @@ __all__ = [
     "paged_attention_v1_workspace_size",
     "paged_attention_v2",
     "paged_prefill_attention",
+    "paged_attention_append_v1",
+    "paged_attention_append_v2",
+    "paged_attention_fp8_v1",
+    "paged_attention_fp8_v2",
+    "reshape_and_cache_fp8",
+    "build_decode_inputs",
     "v2_num_partitions",
     "reshape_and_cache",
     "copy_blocks",
@@ -44,7 +50,8 @@ __all__ = [
 
 V2_PARTITION_TOKENS = 512
 
-_DTYPES = {torch.float32: _lib.CF_F32, torch.float16: _lib.CF_F16, torch.bfloat16: _lib.CF_BF16}
+_DTYPES = {torch.float32: _lib.CF_F32, torch.float16: _lib.CF_F16, torch.bfloat16: _lib.CF_BF16,
+           torch.float8_e4m3fn: _lib.CF_FP8_E4M3}
 
 
 def dtype_code(dt: torch.dtype) -> int:
@@ -63,7 +70,7 @@ def _stream(t: torch.Tensor) -> int:
 
 
 def _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
-                      max_context_len) -> AttentionParams:
+                      max_context_len, fp8: bool = False) -> AttentionParams:
     for name, t in (("out", out), ("query", query), ("key_cache", key_cache),
                     ("value_cache", value_cache), ("block_tables", block_tables),
                     ("context_lens", context_lens)):
@@ -71,7 +78,11 @@ def _attention_params(out, query, key_cache, value_cache, block_tables, context_
             raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, f"{name} must be contiguous")
     if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
         raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "block_tables/context_lens must be int32")
-    if not (query.dtype == key_cache.dtype == value_cache.dtype == out.dtype):
+    if fp8:
+        if not (key_cache.dtype == value_cache.dtype == torch.float8_e4m3fn and query.dtype == out.dtype):
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT,
+                                 "fp8 attention: float8_e4m3fn caches, query and output of one 16-bit dtype")
+    elif not (query.dtype == key_cache.dtype == value_cache.dtype == out.dtype):
         raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "query, caches and output must share a dtype")
     num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
     p = AttentionParams()
@@ -208,6 +219,61 @@ def paged_attention_append_v2(out, exp_sums, max_logits, tmp_output, query, key,
                                            exp_sums.shape[-1], _stream(query)),
           "cf_paged_attention_append_v2")
     return out
+
+
+def paged_attention_fp8_v1(out, query, key_cache, value_cache, block_tables, context_lens, k_scale, v_scale,
+                           scale=None, max_context_len=None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention over float8_e4m3fn caches holding K / k_scale and V / v_scale
+    (query and output f16 or bf16); workspace as paged_attention_v1."""
+    lib = _lib.load()
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len, fp8=True)
+    ws = _ptr(workspace)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib.cf_paged_attention_fp8_v1(ctypes.byref(p), float(k_scale), float(v_scale), ws, ws_bytes,
+                                        _stream(query)),
+          "cf_paged_attention_fp8_v1")
+    return out
+
+
+def paged_attention_fp8_v2(out, exp_sums, max_logits, tmp_output, query, key_cache, value_cache, block_tables,
+                           context_lens, k_scale, v_scale, scale=None, max_context_len=None) -> torch.Tensor:
+    """Partitioned form of paged_attention_fp8_v1 (scratch as paged_attention_v2)."""
+    lib = _lib.load()
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len, fp8=True)
+    for t in (exp_sums, max_logits, tmp_output):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "v2 scratch must be contiguous float32")
+    check(lib.cf_paged_attention_fp8_v2(ctypes.byref(p), float(k_scale), float(v_scale), _ptr(exp_sums),
+                                        _ptr(max_logits), _ptr(tmp_output), exp_sums.shape[-1], _stream(query)),
+          "cf_paged_attention_fp8_v2")
+    return out
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale) -> None:
+    """reshape_and_cache into float8_e4m3fn caches: cache = e4m3(x / scale)."""
+    lib = _lib.load()
+    num_blocks, num_kv_heads, block_size, head_dim = key_cache.shape
+    if slot_mapping.dtype != torch.int32:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "slot_mapping must be int32")
+    if key_cache.dtype != torch.float8_e4m3fn or value_cache.dtype != torch.float8_e4m3fn:
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "caches must be float8_e4m3fn")
+    if not (key.is_contiguous() and value.is_contiguous() and key.dtype == value.dtype):
+        raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "key/value must be contiguous, of one dtype")
+    check(lib.cf_reshape_and_cache_fp8(_ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache),
+                                       _ptr(slot_mapping), key.shape[0], num_kv_heads, head_dim, block_size,
+                                       num_blocks, dtype_code(key.dtype), float(k_scale), float(v_scale),
+                                       _stream(key_cache)),
+          "cf_reshape_and_cache_fp8")
 
 
 def build_decode_inputs(positions, block_offsets, block_ids, max_blocks_per_seq, block_size=16,

@@ -49,7 +49,10 @@ typedef enum cf_status {
 typedef enum cf_dtype {
   CF_F32 = 0,  /* float  (the reference's only type) */
   CF_F16 = 1,  /* IEEE half                          */
-  CF_BF16 = 2  /* bfloat16                           */
+  CF_BF16 = 2, /* bfloat16                           */
+  CF_FP8_E4M3 = 3 /* 8-bit float e4m3 (OCP FP8, finite-only, max 448): KV caches
+                   * only, value = stored * per-cache scale; the block
+                   * operators move it as bytes */
 } cf_dtype;
 
 /* Bits of the per-device error word (cf_get_device_errors). */
@@ -142,6 +145,36 @@ CF_API cf_status cf_paged_attention_append_v2(const cf_paged_attention_params* p
                                               const int32_t* slot_mapping, float* exp_sums,
                                               float* max_logits, float* tmp_output,
                                               int32_t num_partitions, void* stream);
+
+/* Decode attention over fp8 (e4m3) KV caches: the stored values times the
+ * per-cache scales are K and V (K = k_scale * stored, V = v_scale * stored).
+ * params->dtype is the type of the query and the output (CF_F16 or CF_BF16);
+ * head_dim 128 or 256.  Same workspace rules and results as
+ * cf_paged_attention_v1 over the dequantized caches, within the 16-bit
+ * attention tolerance.  Halves the KV bytes of a 16-bit cache.  No reference
+ * counterpart (CacheFlow's caches are fp32); fill such caches with
+ * cf_reshape_and_cache_fp8; cf_copy_blocks / cf_compact_kv_cache /
+ * cf_memset_blocks / cf_swap_blocks take them with dtype CF_FP8_E4M3. */
+CF_API cf_status cf_paged_attention_fp8_v1(const cf_paged_attention_params* params,
+                                           float k_scale, float v_scale, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+
+/* Partitioned form of cf_paged_attention_fp8_v1 (scratch as cf_paged_attention_v2). */
+CF_API cf_status cf_paged_attention_fp8_v2(const cf_paged_attention_params* params,
+                                           float k_scale, float v_scale, float* exp_sums,
+                                           float* max_logits, float* tmp_output,
+                                           int32_t num_partitions, void* stream);
+
+/* cf_reshape_and_cache into fp8 (e4m3) caches: key/value rows of `dtype`
+ * (CF_F32, CF_F16 or CF_BF16) are stored as e4m3(x / scale) -- x / scale
+ * rounded to f32, then to the nearest e4m3 (ties to even), saturating at
+ * +-448.  head_dim a multiple of 16; all four pointers 16-byte aligned. */
+CF_API cf_status cf_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
+                                          void* value_cache, const int32_t* slot_mapping,
+                                          int32_t num_tokens, int32_t num_kv_heads,
+                                          int32_t head_dim, int32_t block_size,
+                                          int64_t num_blocks, int32_t dtype, float k_scale,
+                                          float v_scale, void* stream);
 
 /* Device-side batch preparation.  Builds, on the device, what CacheFlow's
  * BatchDecodeEngine::prepare_kv_cache_inputs (batch_decode.cpp:92-131) builds

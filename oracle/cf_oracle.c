@@ -46,10 +46,46 @@ static double bf16_bits_to_double(uint16_t b) {
   return (double)f;
 }
 
+/* OCP FP8 e4m3 ("E4M3FN"): 1 sign, 4 exponent (bias 7), 3 mantissa bits;
+ * exponent 0 is subnormal (m * 2^-9), S.1111.111 is NaN, no infinities;
+ * largest finite 448 = 1.75 * 2^8. */
+static double e4m3_bits_to_double(uint8_t b) {
+  const int e = (b >> 3) & 15, m = b & 7;
+  double v;
+  if (e == 15 && m == 7)
+    v = NAN;
+  else if (e == 0)
+    v = ldexp((double)m, -9);
+  else
+    v = ldexp((double)(8 + m), e - 10);
+  return (b & 0x80) ? -v : v;
+}
+
+/* Round a float to e4m3: nearest, ties to even; magnitudes from 448 up
+ * (infinities included) saturate to 448; NaN -> 0x7f. */
+uint8_t cfo_e4m3_from_float(float x) {
+  const uint8_t sign = signbit(x) ? 0x80 : 0;
+  if (isnan(x)) return 0x7f;
+  const double a = fabs((double)x);
+  if (a >= 448.0) return sign | 0x7e;
+  if (a < ldexp(1.0, -6)) /* subnormal quantum 2^-9; 8 * 2^-9 is the code of 2^-6 */
+    return sign | (uint8_t)rint(a * 512.0);
+  int e2;
+  frexp(a, &e2);
+  int E = e2 - 1; /* a in [2^E, 2^(E+1)) */
+  double m = rint(ldexp(a, 3 - E)); /* 8..16 */
+  if (m == 16.0) {
+    m = 8.0;
+    ++E;
+  }
+  return sign | (uint8_t)(((E + 7) << 3) | ((int)m - 8));
+}
+
 double cfo_load(const void* base, int64_t index, int32_t dtype) {
   switch (dtype) {
     case 0: return (double)((const float*)base)[index];
     case 1: return half_bits_to_double(((const uint16_t*)base)[index]);
+    case 3: return e4m3_bits_to_double(((const uint8_t*)base)[index]);
     default: return bf16_bits_to_double(((const uint16_t*)base)[index]);
   }
 }
@@ -66,6 +102,8 @@ typedef struct {
   double scale;
   int32_t S, H, Hkv, D, bs, mbps, dtype;
   int32_t next; /* next (seq, head) pair, taken under `mu` */
+  int32_t cdtype;        /* cache element type (dtype unless the caches are fp8) */
+  double kscale, vscale; /* K = kscale * stored, V = vscale * stored */
   pthread_mutex_t mu;
 } attn_job;
 
@@ -79,8 +117,8 @@ static void logits(const attn_job* j, int s, int h, int t0, int t1, double* sc) 
     const int64_t koff = ((phys * j->Hkv + kvh) * j->bs + off) * j->D;
     double dot = 0.0;
     for (int d = 0; d < j->D; ++d)
-      dot += cfo_load(j->q, qoff + d, j->dtype) * cfo_load(j->k, koff + d, j->dtype);
-    sc[t - t0] = dot * j->scale;
+      dot += cfo_load(j->q, qoff + d, j->dtype) * cfo_load(j->k, koff + d, j->cdtype);
+    sc[t - t0] = dot * j->kscale * j->scale;
   }
 }
 
@@ -98,7 +136,7 @@ static void weighted_v(const attn_job* j, int s, int h, int t0, int t1, double* 
     const int blk = t / j->bs, off = t % j->bs;
     const int64_t phys = j->tables[(int64_t)s * j->mbps + blk];
     const int64_t voff = ((phys * j->Hkv + kvh) * j->bs + off) * j->D;
-    for (int d = 0; d < j->D; ++d) o[d] += w * cfo_load(j->v, voff + d, j->dtype);
+    for (int d = 0; d < j->D; ++d) o[d] += w * j->vscale * cfo_load(j->v, voff + d, j->cdtype);
   }
   if (sum > 0)
     for (int d = 0; d < j->D; ++d) o[d] /= sum;
@@ -130,6 +168,8 @@ static void* attn_worker(void* arg) {
   return NULL;
 }
 
+static void run_attention(attn_job* jp, int32_t num_threads);
+
 void cfo_paged_attention(const void* query, const void* key_cache, const void* value_cache,
                          double* out, const int32_t* block_tables, const int32_t* context_lens,
                          float scale, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
@@ -138,6 +178,29 @@ void cfo_paged_attention(const void* query, const void* key_cache, const void* v
   attn_job j = {query, key_cache, value_cache, out, block_tables, context_lens, (double)scale,
                 num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
                 dtype, 0};
+  j.cdtype = dtype;
+  j.kscale = j.vscale = 1.0;
+  run_attention(&j, num_threads);
+}
+
+/* fp8 (e4m3) caches: K = k_scale * stored, V = v_scale * stored; the query
+ * (and the result's type) is `dtype`. */
+void cfo_paged_attention_fp8(const void* query, const void* key_cache, const void* value_cache,
+                             double* out, const int32_t* block_tables, const int32_t* context_lens,
+                             float scale, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t block_size, int32_t max_blocks_per_seq,
+                             int32_t dtype, float k_scale, float v_scale, int32_t num_threads) {
+  attn_job j = {query, key_cache, value_cache, out, block_tables, context_lens, (double)scale,
+                num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
+                dtype, 0};
+  j.cdtype = 3;
+  j.kscale = (double)k_scale;
+  j.vscale = (double)v_scale;
+  run_attention(&j, num_threads);
+}
+
+static void run_attention(attn_job* jp, int32_t num_threads) {
+  attn_job j = *jp;
   pthread_mutex_init(&j.mu, NULL);
   if (num_threads <= 1) {
     attn_worker(&j);
@@ -160,6 +223,8 @@ void cfo_paged_attention_partitions(const void* query, const void* key_cache,
   attn_job j = {query, key_cache, value_cache, NULL, block_tables, context_lens, (double)scale,
                 num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
                 dtype, 0};
+  j.cdtype = dtype;
+  j.kscale = j.vscale = 1.0;
   double* sc = (double*)malloc(sizeof(double) * (size_t)(partition_size > 0 ? partition_size : 1));
   for (int s = 0; s < num_seqs; ++s) {
     const int ctx = context_lens[s];
@@ -302,4 +367,25 @@ int32_t cfo_build_decode_inputs(const int32_t* positions, const int64_t* block_o
     }
   }
   return cut;
+}
+
+/* reshape_and_cache into fp8 caches: element x of the new rows (type `dtype`)
+ * is stored as e4m3(float(x) / scale), the division rounded to float. */
+void cfo_reshape_and_cache_fp8(const void* key, const void* value, uint8_t* key_cache,
+                               uint8_t* value_cache, const int32_t* slot_mapping,
+                               int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t block_size, int32_t dtype, float k_scale, float v_scale) {
+  for (int32_t t = 0; t < num_tokens; ++t) {
+    const int64_t slot = slot_mapping[t];
+    if (slot < 0) continue;
+    const int64_t blk = slot / block_size, off = slot % block_size;
+    for (int32_t h = 0; h < num_kv_heads; ++h) {
+      const int64_t src = ((int64_t)t * num_kv_heads + h) * head_dim;
+      const int64_t dst = ((blk * num_kv_heads + h) * block_size + off) * head_dim;
+      for (int32_t d = 0; d < head_dim; ++d) {
+        key_cache[dst + d] = cfo_e4m3_from_float((float)cfo_load(key, src + d, dtype) / k_scale);
+        value_cache[dst + d] = cfo_e4m3_from_float((float)cfo_load(value, src + d, dtype) / v_scale);
+      }
+    }
+  }
 }

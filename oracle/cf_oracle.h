@@ -7,7 +7,8 @@
  *
  * Each function restates one operator of CacheFlow's CUDA layer
  * (src/cacheflow/cuda/) on host memory, citing the reference lines it
- * follows.  Element types use the C-ABI codes: 0 = f32, 1 = f16, 2 = bf16.
+ * follows.  Element types use the C-ABI codes: 0 = f32, 1 = f16, 2 = bf16,
+ * 3 = e4m3 (caches only).
  * Attention accumulates in double and computes the normalised softmax the
  * reference intends; the cache operators are byte copies.
  */
@@ -64,6 +65,24 @@ void cfo_compact_kv_cache(void* key_cache, void* value_cache, const int32_t* src
 
 void cfo_memset_blocks(void* cache, const int32_t* block_ids, int32_t num_listed,
                        int64_t block_bytes);
+
+/* fp8 (e4m3) caches: K = k_scale * stored, V = v_scale * stored, the query
+ * of element type `dtype`; otherwise as cfo_paged_attention. */
+void cfo_paged_attention_fp8(const void* query, const void* key_cache, const void* value_cache,
+                             double* out, const int32_t* block_tables, const int32_t* context_lens,
+                             float scale, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t block_size, int32_t max_blocks_per_seq,
+                             int32_t dtype, float k_scale, float v_scale, int32_t num_threads);
+
+/* Round to e4m3 (OCP "E4M3FN"): nearest, ties to even, saturating at 448;
+ * NaN -> 0x7f. */
+uint8_t cfo_e4m3_from_float(float x);
+
+/* reshape_and_cache into e4m3 caches: cache = e4m3(float(x) / scale). */
+void cfo_reshape_and_cache_fp8(const void* key, const void* value, uint8_t* key_cache,
+                               uint8_t* value_cache, const int32_t* slot_mapping,
+                               int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t block_size, int32_t dtype, float k_scale, float v_scale);
 
 /* Decode-batch preparation of BatchDecodeEngine::prepare_kv_cache_inputs
  * (batch_decode.cpp:92-131), rows given as CSR block lists: row s at

@@ -54,6 +54,11 @@ def lib() -> ctypes.CDLL:
         L.cfo_swap_blocks.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int64]
         L.cfo_compact_kv_cache.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64]
         L.cfo_memset_blocks.argtypes = [c_void_p, c_void_p, c_int32, c_int64]
+        L.cfo_paged_attention_fp8.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_float] + [c_int32] * 7 + [c_float, c_float, c_int32]
+        L.cfo_e4m3_from_float.restype = ctypes.c_uint8
+        L.cfo_e4m3_from_float.argtypes = [c_float]
+        L.cfo_reshape_and_cache_fp8.argtypes = [c_void_p] * 5 + [c_int32] * 5 + [c_float, c_float]
         L.cfo_build_decode_inputs.restype = c_int32
         L.cfo_build_decode_inputs.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                               c_void_p, c_void_p, c_void_p]
@@ -85,6 +90,44 @@ def paged_attention(q, k_cache, v_cache, block_tables, context_lens, scale, dtyp
     lib().cfo_paged_attention(_p(q), _p(k_cache), _p(v_cache), _p(out), _p(bt), _p(cl), float(scale),
                               S, H, Hkv, D, bs, bt.shape[1], _code(q, dtype_code), num_threads)
     return out
+
+
+def paged_attention_fp8(q, k_cache, v_cache, block_tables, context_lens, scale, k_scale, v_scale,
+                        dtype_code=None, num_threads=1) -> np.ndarray:
+    """float64 attention over e4m3 caches (uint8 arrays): K = k_scale * stored, V = v_scale * stored."""
+    S, H, D = q.shape
+    _, Hkv, bs, _ = k_cache.shape
+    assert k_cache.dtype == np.uint8 and v_cache.dtype == np.uint8
+    out = np.zeros((S, H, D), dtype=np.float64)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    cl = np.ascontiguousarray(context_lens, dtype=np.int32)
+    lib().cfo_paged_attention_fp8(_p(q), _p(k_cache), _p(v_cache), _p(out), _p(bt), _p(cl), float(scale), S, H, Hkv,
+                                  D, bs, bt.shape[1], _code(q, dtype_code), float(k_scale), float(v_scale),
+                                  num_threads)
+    return out
+
+
+def e4m3_from_float(x) -> np.ndarray:
+    """uint8 e4m3 codes of float32 values (nearest, ties to even, saturating at 448)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    f = lib().cfo_e4m3_from_float
+    return np.array([f(float(v)) for v in x.reshape(-1)], np.uint8).reshape(x.shape)
+
+
+def e4m3_to_float(codes) -> np.ndarray:
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    f = lib().cfo_load
+    return np.array([f(c.ctypes.data, i, 3) for i in range(c.size)], np.float64).reshape(c.shape)
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale,
+                          dtype_code=None) -> None:
+    """In place on uint8 key_cache / value_cache."""
+    T, Hkv, D = key.shape
+    bs = key_cache.shape[2]
+    sm = np.ascontiguousarray(slot_mapping, dtype=np.int32)
+    lib().cfo_reshape_and_cache_fp8(_p(key), _p(value), _p(key_cache), _p(value_cache), _p(sm), T, Hkv, D, bs,
+                                    _code(key, dtype_code), float(k_scale), float(v_scale))
 
 
 def paged_attention_partitions(q, k_cache, v_cache, block_tables, context_lens, scale,

@@ -1,0 +1,170 @@
+"""FP8 (e4m3) KV caches: the quantizing scatter (cf_reshape_and_cache_fp8) is
+bit-exact against the oracle's rounding, and decode attention over fp8 caches
+(cf_paged_attention_fp8_v1/_v2, FMA and tensor-core consumers) matches the
+oracle's attention over the dequantized caches within the 16-bit tolerance."""
+
+import math
+
+import numpy as np
+import pytest
+
+from cacheflow_b200.workloads import host_values
+from helpers import CODE, as_f64, assert_close, random_tables, to_dev, torch_dtype
+
+pytestmark = pytest.mark.gpu
+
+K_SCALE, V_SCALE = 0.05, 0.1
+
+
+def _fp8_cache(rng, shape):
+    """Random e4m3 codes from N(0, 1) values (no NaN codes)."""
+    import torch
+
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * 2)
+    return x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def _to_fp8_dev(codes):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(codes)).cuda().view(torch.float8_e4m3fn)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_reshape_and_cache_fp8_bit_exact(cflib, oracle_mod, dtype):
+    import torch
+
+    from cacheflow_b200 import ops
+    from helpers import to_host
+
+    rng = np.random.default_rng(12)
+    T, Hkv, D, pool = 300, 8, 128, 64
+    key = host_values((T, Hkv, D), dtype, 20.0, rng)   # reaches past 448 * scale: saturation
+    val = host_values((T, Hkv, D), dtype, 0.02, rng)   # small: subnormal codes
+    slots = rng.permutation(pool * 16)[:T].astype(np.int32)
+    slots[::37] = -1
+    kc = np.zeros((pool, Hkv, 16, D), np.uint8)
+    vc = np.zeros_like(kc)
+    dk, dv = _to_fp8_dev(kc), _to_fp8_dev(vc)
+    ops.reshape_and_cache_fp8(to_dev(key, dtype), to_dev(val, dtype), dk, dv, to_dev(slots), K_SCALE, V_SCALE)
+    oracle_mod.reshape_and_cache_fp8(key, val, kc, vc, slots, K_SCALE, V_SCALE, CODE[dtype])
+    assert np.array_equal(dk.view(torch.uint8).cpu().numpy(), kc)
+    assert np.array_equal(dv.view(torch.uint8).cpu().numpy(), vc)
+    assert ops.device_errors(0) == 0
+
+
+CASES = [
+    # query dtype, num_heads, num_kv_heads, head_dim, contexts
+    ("f16", 8, 8, 128, [1, 15, 16, 17, 129, 512, 513, 3000]),
+    ("bf16", 32, 8, 128, [1, 16, 17, 700, 1025, 9000]),   # group 4: tensor-core consumer
+    ("bf16", 32, 2, 128, [3, 160, 1030]),                 # group 16: two head chunks
+    ("f16", 8, 4, 128, [5, 300]),                         # group 2
+    ("bf16", 8, 8, 256, [1, 17, 300]),
+    ("f16", 16, 2, 256, [1, 100, 1500]),
+]
+
+
+@pytest.fixture(params=["auto", "fma", "mma"])
+def consumer(request, monkeypatch):
+    if request.param == "auto":
+        monkeypatch.delenv("CF_ATTN_CONSUMER", raising=False)
+    else:
+        monkeypatch.setenv("CF_ATTN_CONSUMER", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("path", ["v1", "v1_split", "v2"])
+@pytest.mark.parametrize("dtype,H,Hkv,D,ctx", CASES)
+def test_fp8_attention_matches_oracle(cflib, oracle_mod, consumer, path, dtype, H, Hkv, D, ctx):
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(hash((dtype, H, Hkv, D, len(ctx), path)) % 2**32)
+    S = len(ctx)
+    pool = sum((c + 15) // 16 for c in ctx) + 5
+    tables = random_tables(rng, ctx, pool)
+    cl = np.array(ctx, np.int32)
+    q = host_values((S, H, D), dtype, 0.5, rng)
+    kc, vc = _fp8_cache(rng, (pool, Hkv, 16, D)), _fp8_cache(rng, (pool, Hkv, 16, D))
+    dq, dk, dv = to_dev(q, dtype), _to_fp8_dev(kc), _to_fp8_dev(vc)
+    bt, dcl = to_dev(tables), to_dev(cl)
+    out = torch.full((S, H, D), 5.0, dtype=torch_dtype(dtype), device="cuda")
+    mctx = int(cl.max())
+    if path == "v2":
+        P = ops.v2_num_partitions(mctx)
+        es = torch.empty((S, H, P), device="cuda")
+        ml = torch.empty_like(es)
+        to = torch.empty((S, H, P, D), device="cuda")
+        ops.paged_attention_fp8_v2(out, es, ml, to, dq, dk, dv, bt, dcl, K_SCALE, V_SCALE)
+    else:
+        ws = None
+        if path == "v1_split":
+            n = ops.paged_attention_v1_workspace_size(dq, dk, bt, mctx)
+            ws = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda") if n else None
+        ops.paged_attention_fp8_v1(out, dq, dk, dv, bt, dcl, K_SCALE, V_SCALE, workspace=ws)
+    want = oracle_mod.paged_attention_fp8(q, kc, vc, tables, cl, 1 / math.sqrt(D), K_SCALE, V_SCALE, CODE[dtype],
+                                          num_threads=8)
+    assert_close(as_f64(out), want, dtype, f"fp8 attention {path}")
+    assert ops.device_errors(0) == 0
+
+
+def test_fp8_nan_codes_past_context_do_not_leak(cflib, oracle_mod, consumer):
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(14)
+    ctx = [20, 33, 7]
+    tables = random_tables(rng, ctx, 12)
+    cl = np.array(ctx, np.int32)
+    q = host_values((3, 32, 128), "bf16", 0.5, rng)
+    kc, vc = _fp8_cache(rng, (12, 8, 16, 128)), _fp8_cache(rng, (12, 8, 16, 128))
+    for s, c in enumerate(ctx):
+        b = tables[s][c // 16]
+        kc[b, :, c % 16:] = 0x7F   # e4m3 NaN
+        vc[b, :, c % 16:] = 0xFF
+    out = torch.empty((3, 32, 128), dtype=torch.bfloat16, device="cuda")
+    ops.paged_attention_fp8_v1(out, to_dev(q, "bf16"), _to_fp8_dev(kc), _to_fp8_dev(vc), to_dev(tables),
+                               to_dev(cl), K_SCALE, V_SCALE)
+    want = oracle_mod.paged_attention_fp8(q, kc, vc, tables, cl, 1 / math.sqrt(128), K_SCALE, V_SCALE, CODE["bf16"])
+    assert_close(as_f64(out), want, "bf16", "fp8 with NaN codes past the context")
+
+
+def test_fp8_caches_move_as_bytes(cflib):
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(15)
+    kc = _to_fp8_dev(_fp8_cache(rng, (20, 8, 16, 128)))
+    vc = _to_fp8_dev(_fp8_cache(rng, (20, 8, 16, 128)))
+    k0, v0 = kc.view(torch.uint8).clone(), vc.view(torch.uint8).clone()
+    pairs = torch.tensor([[1, 5], [7, 2]], dtype=torch.int64, device="cuda")
+    ops.copy_blocks(kc, vc, pairs)
+    ku = kc.view(torch.uint8)
+    assert torch.equal(ku[5], k0[1]) and torch.equal(ku[2], k0[7]) and torch.equal(ku[0], k0[0])
+    ops.memset_blocks(kc, torch.tensor([3], dtype=torch.int32, device="cuda"))
+    assert int(kc.view(torch.uint8)[3].count_nonzero()) == 0
+    ops.compact_kv_cache(kc, vc, torch.tensor([9], dtype=torch.int32, device="cuda"),
+                         torch.tensor([4], dtype=torch.int32, device="cuda"))
+    assert torch.equal(vc.view(torch.uint8)[4], v0[9])
+
+
+def test_fp8_rejects_unsupported(cflib):
+    import torch
+
+    from cacheflow_b200 import _lib, ops
+
+    q = torch.zeros((1, 8, 64), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((2, 8, 16, 64), dtype=torch.float8_e4m3fn, device="cuda")
+    bt = torch.zeros((1, 1), dtype=torch.int32, device="cuda")
+    cl = torch.ones(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(ops.CacheFlowError) as e:  # head_dim 64
+        ops.paged_attention_fp8_v1(torch.empty_like(q), q, kc, kc, bt, cl, 1.0, 1.0)
+    assert e.value.status == _lib.CF_ERR_UNSUPPORTED
+    q = torch.zeros((1, 8, 128), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((2, 8, 16, 128), dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(ops.CacheFlowError) as e:  # scale must be finite and > 0
+        ops.paged_attention_fp8_v1(torch.empty_like(q), q, kc, kc, bt, cl, 0.0, 1.0)
+    assert e.value.status == _lib.CF_ERR_INVALID_ARGUMENT

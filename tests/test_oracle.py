@@ -220,3 +220,74 @@ def test_build_decode_inputs_edge_cases(oracle_mod):
     assert ctx.tolist() == [0, 1, 41, 6, 101]
     assert slots.tolist() == [-1, 102 * 16, 105 * 16 + 8, 106 * 16 + 5, -1]
     assert tables[3].tolist() == [106, 107, 108, 109] and tables[1].tolist() == [102, 0, 0, 0]
+
+
+def test_e4m3_codec_matches_torch(oracle_mod):
+    """The oracle's e4m3 decoding of all 256 codes and its rounding (nearest,
+    ties to even) agree with torch.float8_e4m3fn, an independent
+    implementation of the OCP format; saturation is the oracle's own rule."""
+    import torch
+
+    codes = np.arange(256, dtype=np.uint8)
+    ours = oracle_mod.e4m3_to_float(codes)
+    theirs = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy().astype(np.float64)
+    assert np.array_equal(np.isnan(ours), np.isnan(theirs))
+    ok = ~np.isnan(ours)
+    assert np.array_equal(ours[ok], theirs[ok])
+    # values: random magnitudes over the whole range, exact codes, midpoints
+    # between neighbouring codes (ties), subnormals, signed zeros
+    rng = np.random.default_rng(8)
+    finite = np.sort(np.unique(np.abs(ours[ok])))
+    mids = (finite[:-1] + finite[1:]) / 2
+    x = np.concatenate([
+        rng.uniform(-447.9, 447.9, 3000), rng.standard_normal(3000) * 0.01, finite, -finite, mids, -mids,
+        rng.uniform(0, 2 ** -6, 500), [0.0, -0.0],
+    ]).astype(np.float32)
+    x = x[np.abs(x) < 448]
+    got = oracle_mod.e4m3_from_float(x)
+    want = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(got, want)
+    # saturation (the kernels' satfinite conversion): +-448 and beyond, infinities
+    big = np.array([448.0, 449.0, 464.0, 500.0, 1e30, np.inf], np.float32)
+    assert np.all(oracle_mod.e4m3_from_float(big) == 0x7E)
+    assert np.all(oracle_mod.e4m3_from_float(-big) == 0xFE)
+
+
+@pytest.mark.parametrize("qdtype", ["f16", "bf16"])
+def test_fp8_attention_oracle_equals_dequantized_attention(oracle_mod, qdtype):
+    rng = np.random.default_rng(9)
+    ctx = [1, 16, 17, 300]
+    S, H, Hkv, D = len(ctx), 8, 2, 128
+    pool = sum((c + 15) // 16 for c in ctx) + 3
+    tables = random_tables(rng, ctx, pool)
+    q = host_values((S, H, D), qdtype, 0.5, rng)
+    codes = rng.integers(0, 256, (2, pool, Hkv, 16, D)).astype(np.uint8)
+    codes[(codes & 0x7F) == 0x7F] = 0x3C  # no NaN codes
+    kc, vc = codes[0], codes[1]
+    ks, vs = 0.02, 0.05
+    got = oracle_mod.paged_attention_fp8(q, kc, vc, tables, np.array(ctx, np.int32), 1 / math.sqrt(D), ks, vs,
+                                         CODE[qdtype])
+    # the scales reach the oracle as float32
+    kd = oracle_mod.e4m3_to_float(kc) * float(np.float32(ks))
+    vd = oracle_mod.e4m3_to_float(vc) * float(np.float32(vs))
+    qd = oracle_mod.to_f64(q, CODE[qdtype])
+    want = oracle_mod.paged_attention_numpy(qd, kd, vd, tables, np.array(ctx, np.int32), 1 / math.sqrt(D))
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_fp8_reshape_oracle(oracle_mod):
+    rng = np.random.default_rng(10)
+    T, Hkv, D, pool = 6, 2, 32, 4
+    key = host_values((T, Hkv, D), "bf16", 3.0, rng)
+    val = host_values((T, Hkv, D), "bf16", 3.0, rng)
+    kc = np.zeros((pool, Hkv, 16, D), np.uint8)
+    vc = np.zeros_like(kc)
+    slots = np.array([0, 17, 33, -1, 63, 5], np.int32)
+    oracle_mod.reshape_and_cache_fp8(key, val, kc, vc, slots, 0.5, 0.25, CODE["bf16"])
+    kf = oracle_mod.to_f64(key, CODE["bf16"]).astype(np.float32)
+    for t, s in enumerate(slots):
+        if s < 0:
+            continue
+        want = oracle_mod.e4m3_from_float(kf[t] / np.float32(0.5))
+        assert np.array_equal(kc[s // 16, :, s % 16], want)
+    assert not kc[0, :, 1:5].any()
