@@ -128,6 +128,18 @@ def fill_normal_(t, std, gen):
     return t.normal_(0.0, std, generator=gen)
 
 
+def fill_fp8_(t, std, scale, gen, chunk=1 << 28):
+    """float8_e4m3fn cache of N(0, std) values stored as e4m3(x / scale)."""
+    import torch
+
+    flat = t.view(-1)
+    for i in range(0, flat.numel(), chunk):
+        n = min(chunk, flat.numel() - i)
+        x = torch.empty(n, dtype=torch.float32, device=t.device).normal_(0.0, std, generator=gen)
+        flat[i:i + n] = (x / scale).to(torch.float8_e4m3fn)
+    return t
+
+
 SHARDED = {"llama3_70b_sharded"}
 L2_BYTES = 126 * 1024 * 1024
 L2_FLUSH_BYTES = 512 * 1024 * 1024
@@ -234,10 +246,20 @@ def run_ours(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
     S, H, Hkv, D = w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim
-    k_cache = torch.empty(w.cache_shape(), dtype=tdt, device=dev)
-    v_cache = torch.empty_like(k_cache)
-    fill_normal_(k_cache, w.std, gen)
-    fill_normal_(v_cache, w.std, gen)
+    fp8 = args.kv_dtype == "fp8"
+    if fp8 and (w.dtype == "f32" or w.has_chunks):
+        raise SystemExit("--kv-dtype fp8 needs a 16-bit decode-only workload")
+    kv_scale = w.std / 64.0  # N(0, std) / scale: 7 sigma reaches the e4m3 maximum (448)
+    if fp8:
+        k_cache = torch.empty(w.cache_shape(), dtype=torch.float8_e4m3fn, device=dev)
+        v_cache = torch.empty_like(k_cache)
+        fill_fp8_(k_cache, w.std, kv_scale, gen)
+        fill_fp8_(v_cache, w.std, kv_scale, gen)
+    else:
+        k_cache = torch.empty(w.cache_shape(), dtype=tdt, device=dev)
+        v_cache = torch.empty_like(k_cache)
+        fill_normal_(k_cache, w.std, gen)
+        fill_normal_(v_cache, w.std, gen)
     T = len(w.slot_mapping)
     q = torch.empty((S, H, D), dtype=tdt, device=dev).normal_(0, w.std, generator=gen)
     k_new = torch.empty((T, Hkv, D), dtype=tdt, device=dev).normal_(0, w.std, generator=gen)
@@ -252,16 +274,17 @@ def run_ours(args):
     nc = len(w.chunk_context_lens) if chunked else 0
     # decode-only batches (one new token per row, at its newest position)
     # append it inside the attention launch unless --append separate
-    fused = args.append == "fused" and not w.has_chunks and T == S
+    fused = args.append == "fused" and not w.has_chunks and T == S and not fp8
     new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
-                          max_chunks=nc, fused_append=fused)
+                          max_chunks=nc, fused_append=fused, kv_scales=(kv_scale, kv_scale) if fp8 else None,
+                          query_dtype=tdt)
     engine.q[:S].copy_(q)
     engine.tables.copy_(tables)
     engine.ctx.copy_(ctx)
     stream = engine.stream
     chunks = None
-    kv_step = w.kv_bytes()
+    kv_step = w.kv_bytes() // w.elem_bytes if fp8 else w.kv_bytes()  # fp8: one byte per element
     if chunked:
         # decode rows [0, num_decode) through paged attention, the prefill
         # chunks' tokens through the multi-query operator
@@ -282,7 +305,9 @@ def run_ours(args):
     def step(record=False):
         if pairs is not None:
             ops.copy_blocks(k_cache, v_cache, pairs)
-        if not fused:
+        if fp8:
+            ops.reshape_and_cache_fp8(k_new, v_new, k_cache, v_cache, slots, kv_scale, kv_scale)
+        elif not fused:
             ops.reshape_and_cache(k_new, v_new, k_cache, v_cache, slots)
         if record:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -372,7 +397,7 @@ def run_ours(args):
         raise RuntimeError("device error word set during the timed region")
 
     pool_ops = None
-    if args.workload in SHARDED and not args.no_pool_ops:
+    if args.workload in SHARDED and not args.no_pool_ops and not fp8:
         with torch.cuda.stream(stream):
             pool_ops = time_pool_ops(w, k_cache, v_cache, world, args.swap_gb)
         keys = sorted(pool_ops)
@@ -429,16 +454,19 @@ def run_ours(args):
                 "v1_split": args.v1_split,
                 "append": ("new K/V appended inside the attention launch" if fused
                            else "reshape_and_cache launch before attention"),
+                "kv_dtype": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % kv_scale
+                             if fp8 else w.dtype),
                 "l2": ("L2 flushed before every timed step (512 MB write, outside the step's events)"
                        if flush is not None else
-                       "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (w.kv_bytes() / 1e9)),
-                "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes(),
+                       "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (kv_step / 1e9)),
+                "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes() // (w.elem_bytes if fp8 else 1),
                 "parallelism": (f"dp{world} (one global batch, sequences dealt to per-GPU pools by LPT)"
                                 if scaling == "strong" else
                                 f"dp{world} (per-GPU pools and batches, no data-path collective)"),
             },
             "tokens_per_s": round(seqs_total / (ms_step * 1e-3), 1),
-            "unique_kv_GBps": round(world * w.unique_kv_bytes() / (ms_step * 1e-3) / 1e9, 1),
+            "unique_kv_GBps": round(world * w.unique_kv_bytes() / (w.elem_bytes if fp8 else 1)
+                                    / (ms_step * 1e-3) / 1e9, 1),
             "frac_of_hbm_peak": round(value / (peak * world), 4),
             "roofline": {
                 "bound": "hbm",
@@ -451,7 +479,7 @@ def run_ours(args):
                 "peak_source": peak_kind,
                 "alg_bytes_per_launch": alg_bytes,
                 "kernel_ms": round(att_ms, 4),
-                "traffic": traffic_from_profiles(w.name),
+                "traffic": traffic_from_profiles(w.name + ("_fp8" if fp8 else "")),
             },
             "e2e": {
                 "value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 1),
@@ -585,6 +613,8 @@ def main():
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--kv-dtype", choices=["native", "fp8"], default="native",
+                    help="KV cache element type: the workload's own, or fp8 e4m3 with a per-cache scale")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="decode batches: append the new K/V inside the attention launch, or run "
                          "reshape_and_cache before it")

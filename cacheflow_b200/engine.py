@@ -49,7 +49,11 @@ class DecodeEngine:
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, num_heads: int,
                  max_seqs: int, max_blocks_per_seq: int, max_new_tokens: int | None = None,
                  stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2,
-                 max_chunks: int = 0, fused_append: bool = False):
+                 max_chunks: int = 0, fused_append: bool = False, kv_scales: tuple[float, float] | None = None,
+                 query_dtype: torch.dtype | None = None):
+        """kv_scales = (k_scale, v_scale) with float8_e4m3fn caches: the caches
+        hold K / k_scale and V / v_scale; queries, new K/V rows and outputs are
+        `query_dtype` (f16 / bf16)."""
         self.k = key_cache
         self.v = value_cache
         self.device = key_cache.device
@@ -61,7 +65,11 @@ class DecodeEngine:
         self.stream = stream or torch.cuda.current_stream(self.device)
         self.h2d = torch.cuda.Stream(self.device)
         self.d2h = torch.cuda.Stream(self.device)
-        dt, dev = key_cache.dtype, self.device
+        self.fp8 = key_cache.dtype == torch.float8_e4m3fn
+        if self.fp8 and (kv_scales is None or query_dtype is None):
+            raise ValueError("fp8 caches need kv_scales and query_dtype")
+        self.kv_scales = kv_scales
+        dt, dev = (query_dtype if self.fp8 else key_cache.dtype), self.device
         self.slots_ = [_Slot(max_seqs, self.max_new_tokens, num_heads, self.num_kv_heads, self.head_dim,
                              max_blocks_per_seq, dt, dev, max_chunks) for _ in range(max(1, depth))]
         self.c_tables, self.c_ctx, self.c_start = self.slots_[0].c_tables, self.slots_[0].c_ctx, self.slots_[0].c_start
@@ -99,6 +107,21 @@ class DecodeEngine:
         """new = (k_new, v_new, slot_mapping) of one token per row appends it
         in the same launch."""
         S = num_seqs
+        if self.fp8:
+            ks, vs = self.kv_scales
+            if new is not None:
+                ops.reshape_and_cache_fp8(new[0], new[1], self.k, self.v, new[2], ks, vs)
+            if max_context_len <= V1_MAX_CONTEXT:
+                ops.paged_attention_fp8_v1(out, q, self.k, self.v, bt, cl, ks, vs, None, max_context_len,
+                                           workspace=self.workspace)
+                split = self.workspace is not None and ops.paged_attention_v1_workspace_size(
+                    q, self.k, bt, max_context_len) > 0
+                self.launches_per_step = (2 if split else 1) + (1 if new is not None else 0)
+            else:
+                ops.paged_attention_fp8_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q,
+                                           self.k, self.v, bt, cl, ks, vs, None, max_context_len)
+                self.launches_per_step = 2 + (1 if new is not None else 0)
+            return
         if max_context_len <= V1_MAX_CONTEXT:
             if new is None:
                 ops.paged_attention_v1(out, q, self.k, self.v, bt, cl, None, max_context_len,
@@ -182,10 +205,14 @@ class DecodeEngine:
         self.stream.wait_event(b.h2d_done)
         if b.used:
             self.stream.wait_event(b.d2h_done)  # the slot's output was copied out
-        fused = self.fused_append and chunks_host is None and T == S
+        fused = (self.fused_append or self.fp8) and chunks_host is None and T == S
         with torch.cuda.stream(self.stream):
             if not fused:
-                ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
+                if self.fp8:
+                    ops.reshape_and_cache_fp8(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T],
+                                              *self.kv_scales)
+                else:
+                    ops.reshape_and_cache(b.k_new[:T], b.v_new[:T], self.k, self.v, b.slots[:T])
             if chunks_host is not None:
                 nd, qs, cc, _ = chunks_host
                 max_q = int((qs[1:] - qs[:-1]).max()) if cc.shape[0] else 0

@@ -65,3 +65,48 @@ def test_engine_steps_fused_and_separate(cflib, oracle_mod, dtype, H, Hkv, D, ct
         want = oracle_mod.paged_attention(qs[i], k, v, tables, cl, 1 / math.sqrt(D), CODE[dtype], num_threads=4)
         assert_close(as_f64(o_fus[i]), want, dtype, f"engine step {i}")
     assert np.array_equal(k, k_fus) and np.array_equal(v, v_fus)
+
+
+@pytest.mark.parametrize("dtype,H,Hkv,D,ctx", [
+    ("f16", 8, 8, 128, [1, 17, 300, 2000]),
+    ("bf16", 32, 8, 128, [5, 16, 9000, 700]),
+])
+def test_engine_steps_fp8_caches(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+    import torch
+
+    from cacheflow_b200.engine import DecodeEngine
+
+    rng = np.random.default_rng(19)
+    S, steps, ks, vs = len(ctx), 3, 0.01, 0.02
+    pool = sum((c + steps + 15) // 16 for c in ctx) + 4
+    tables = random_tables(rng, [c + steps for c in ctx], pool)
+    x = torch.from_numpy(rng.standard_normal((2, pool, Hkv, 16, D)).astype(np.float32) * 50)
+    codes = x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    k, v = codes[0].copy(), codes[1].copy()
+    dk = torch.from_numpy(k.copy()).cuda().view(torch.float8_e4m3fn)
+    dv = torch.from_numpy(v.copy()).cuda().view(torch.float8_e4m3fn)
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    eng = DecodeEngine(dk, dv, H, S, tables.shape[1], S, kv_scales=(ks, vs), query_dtype=tdt)
+    outs = []
+    steps_in = []
+    for i in range(steps):
+        cl = np.array(ctx, np.int32) + i + 1
+        pos = cl - 1
+        slots = (tables[np.arange(S), pos // 16] * 16 + pos % 16).astype(np.int32)
+        q = host_values((S, H, D), dtype, 0.5, rng)
+        nk = host_values((S, Hkv, D), dtype, 0.5, rng)
+        nv = host_values((S, Hkv, D), dtype, 0.5, rng)
+        pin = [torch.from_numpy(a).pin_memory() for a in (q, nk, nv, slots, tables, cl)]
+        if dtype == "bf16":
+            pin[:3] = [t.view(torch.bfloat16) for t in pin[:3]]
+        o = torch.empty(pin[0].shape, dtype=tdt).pin_memory()
+        eng.step(*pin, o, int(cl.max()))
+        outs.append(o)
+        steps_in.append((q, nk, nv, slots, cl))
+    eng.synchronize()
+    for i, (q, nk, nv, slots, cl) in enumerate(steps_in):
+        oracle_mod.reshape_and_cache_fp8(nk, nv, k, v, slots, ks, vs, CODE[dtype])
+        want = oracle_mod.paged_attention_fp8(q, k, v, tables, cl, 1 / math.sqrt(D), ks, vs, CODE[dtype],
+                                              num_threads=4)
+        assert_close(as_f64(outs[i]), want, dtype, f"fp8 engine step {i}")
+    assert np.array_equal(dk.view(torch.uint8).cpu().numpy(), k)
