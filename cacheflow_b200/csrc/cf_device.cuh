@@ -43,6 +43,15 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
   return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
+// Four e4m3 (one 32-bit word, low byte first) -> two f16x2: bytes 0-1 in
+// `lo`, bytes 2-3 in `hi`; exact.
+__device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
 // Two floats -> two e4m3 (low byte first): round to nearest even, values
 // beyond the largest finite (448) saturate to it.
 __device__ __forceinline__ uint16_t f2_to_e4m3x2(float x, float y) {

@@ -430,14 +430,14 @@ struct MmaConsumerFp8 {
 #pragma unroll
       for (int kc = 0; kc < kKC; kc += 2) {
         const int c = kc + (mi & 1);
-        uint32_t x0, x1, x2, x3;
-        ldmatrix_x4(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), x0, x1, x2, x3);
-        mma_16816<__half>(s[0], qa[kc][0], 0u, qa[kc][1], 0u, e4m3x2_to_h2(x0), e4m3x2_to_h2(x0 >> 16));
-        mma_16816<__half>(s[1], qa[kc][0], 0u, qa[kc][1], 0u, e4m3x2_to_h2(x2), e4m3x2_to_h2(x2 >> 16));
-        mma_16816<__half>(s[0], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, e4m3x2_to_h2(x1),
-                          e4m3x2_to_h2(x1 >> 16));
-        mma_16816<__half>(s[1], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, e4m3x2_to_h2(x3),
-                          e4m3x2_to_h2(x3 >> 16));
+        uint32_t x[4], b[4][2];
+        ldmatrix_x4(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), x[0], x[1], x[2], x[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) e4m3x4_to_h2x2(x[i], b[i][0], b[i][1]);
+        mma_16816<__half>(s[0], qa[kc][0], 0u, qa[kc][1], 0u, b[0][0], b[0][1]);
+        mma_16816<__half>(s[1], qa[kc][0], 0u, qa[kc][1], 0u, b[2][0], b[2][1]);
+        mma_16816<__half>(s[0], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, b[1][0], b[1][1]);
+        mma_16816<__half>(s[1], qa[kc + 1][0], 0u, qa[kc + 1][1], 0u, b[3][0], b[3][1]);
       }
     }
     float bm = -INFINITY;
@@ -465,12 +465,14 @@ struct MmaConsumerFp8 {
         ps += s[nt][j];
       }
     l = l * alpha + ps;
+    if (__any_sync(0xffffffffu, alpha != 1.f)) {  // the running max moved for some row
 #pragma unroll
-    for (int n = 0; n < kND; ++n) {
-      o[n][0] *= alpha;
-      o[n][1] *= alpha;
-      o[n][2] *= alpha;
-      o[n][3] *= alpha;
+      for (int n = 0; n < kND; ++n) {
+        o[n][0] *= alpha;
+        o[n][1] *= alpha;
+        o[n][2] *= alpha;
+        o[n][3] *= alpha;
+      }
     }
     uint32_t pa[4];
     split2<__half>(s[0][0], s[0][1], pa[0], pa[1]);
@@ -496,17 +498,18 @@ struct MmaConsumerFp8 {
 #pragma unroll
       for (int cp = 0; cp < kKC / 2; ++cp) {
         const int c = 2 * cp + (mi >> 1);
-        uint32_t y0, y1, y2, y3;
-        ldmatrix_x4_trans(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), y0, y1, y2, y3);
-        // chunk 2cp: tokens 0-7 in y0, 8-15 in y1; chunk 2cp+1: y2, y3.
-        mma_16816<__half>(o[4 * cp + 0], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y0, 0, 0x20)),
-                          e4m3x2_to_h2(__byte_perm(y1, 0, 0x20)));
-        mma_16816<__half>(o[4 * cp + 1], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y0, 0, 0x31)),
-                          e4m3x2_to_h2(__byte_perm(y1, 0, 0x31)));
-        mma_16816<__half>(o[4 * cp + 2], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y2, 0, 0x20)),
-                          e4m3x2_to_h2(__byte_perm(y3, 0, 0x20)));
-        mma_16816<__half>(o[4 * cp + 3], pa[0], pa[1], pa[2], pa[3], e4m3x2_to_h2(__byte_perm(y2, 0, 0x31)),
-                          e4m3x2_to_h2(__byte_perm(y3, 0, 0x31)));
+        uint32_t y[4];
+        ldmatrix_x4_trans(rowa + (c >> 3) * kBoxBytes + (((c & 7) ^ (r & 7)) << 4), y[0], y[1], y[2], y[3]);
+        // chunk 2cp: tokens 0-7 in y0, 8-15 in y1; chunk 2cp+1: y2, y3.  One
+        // byte permute gathers a column's 4 tokens (b0 pair, b1 pair).
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t be0, be1, bo0, bo1;
+          e4m3x4_to_h2x2(__byte_perm(y[2 * h], y[2 * h + 1], 0x6420), be0, be1);
+          e4m3x4_to_h2x2(__byte_perm(y[2 * h], y[2 * h + 1], 0x7531), bo0, bo1);
+          mma_16816<__half>(o[4 * cp + 2 * h], pa[0], pa[1], pa[2], pa[3], be0, be1);
+          mma_16816<__half>(o[4 * cp + 2 * h + 1], pa[0], pa[1], pa[2], pa[3], bo0, bo1);
+        }
       }
     }
   }
@@ -610,7 +613,8 @@ template <typename T, int D, int HG>
 struct AttnConfig {
   static constexpr int kTileBytes = kBlockTokens * D * (int)sizeof(T);  // one K or V tile
   static constexpr int kWarps = 4;
-  static constexpr int kStageBudget = 96 * 1024;
+  // 1-byte (fp8) tiles: half the ring, so twice the CTAs fit on an SM.
+  static constexpr int kStageBudget = sizeof(T) == 1 ? 48 * 1024 : 96 * 1024;
   static constexpr int kStagesRaw = kStageBudget / (kWarps * 2 * kTileBytes);
   static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
   static constexpr int kTileArea = kWarps * kStages * 2 * kTileBytes;
@@ -621,10 +625,12 @@ struct AttnConfig {
   static constexpr int kPbufOffset = kFlagOffset + ((kWarps * kStages * 4 + 15) / 16) * 16;
   static constexpr int kSmemBytes = kPbufOffset + kWarps * HG * kBlockTokens * 4;
   static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
+  // fp8 at D=128: four CTAs (16 warps) per SM, the registers capped to fit.
+  static constexpr int kMinCtas = (sizeof(T) == 1 && D == 128) ? 4 : 1;
 };
 
 template <typename T, typename TC, int D, int HG, bool kMma, bool kAppend>
-__global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32)
+__global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig<TC, D, HG>::kMinCtas)
     paged_attention_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv) {
   // T: query / output type; TC: cache type (T, or fp8 e4m3 with T 16-bit).
@@ -1025,7 +1031,8 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
 }
 
 // Which consumer runs: tensor cores for GQA groups of 3+ query heads on 16-bit
-// caches (fp8 caches: head_dim a multiple of 128), FMA otherwise.
+// caches and for every group on fp8 caches (head_dim a multiple of 128), FMA
+// otherwise.
 // CF_ATTN_CONSUMER=fma|mma overrides (read per call).
 bool use_mma(const cf_paged_attention_params& p, int64_t rows, bool fp8) {
   if (p.dtype == CF_F32 || p.num_blocks <= 0 || rows > INT32_MAX) return false;
@@ -1034,7 +1041,8 @@ bool use_mma(const cf_paged_attention_params& p, int64_t rows, bool fp8) {
     if (std::strcmp(e, "fma") == 0) return false;
     if (std::strcmp(e, "mma") == 0) return true;
   }
-  return p.num_heads / p.num_kv_heads >= 3;
+  // fp8 tiles cost the FMA consumer more conversion work than HBM time.
+  return fp8 || p.num_heads / p.num_kv_heads >= 3;
 }
 
 template <typename T, typename TC, int D, bool kAppend>
