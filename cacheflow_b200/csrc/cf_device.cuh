@@ -43,6 +43,15 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
   return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22; results below 2^-126 flush to 0, which a softmax weight that
+// small can afford).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Four e4m3 (one 32-bit word, low byte first) -> two f16x2: bytes 0-1 in
 // `lo`, bytes 2-3 in `hi`; exact.
 __device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {

@@ -377,10 +377,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 namespace {
 
 constexpr int kTcRows = 128;
-constexpr int kTcThreads = 6 * 32;
-constexpr int kTcProducerWarp = 4;
-constexpr int kTcMmaWarp = 5;
-constexpr int kTcStages = 3;
+constexpr int kTcSoftmaxWarps = 8;  // two per 32-row lane quarter: one per half of a stage's keys
+constexpr int kTcThreads = (kTcSoftmaxWarps + 2) * 32;
+constexpr int kTcProducerWarp = 8;
+constexpr int kTcMmaWarp = 9;
+constexpr int kTcStages = 4;
 constexpr int kTcStageKeys = kStageBlocks * kPBlock;  // 64
 constexpr uint32_t kTcTmemCols = 256;
 constexpr uint32_t kTcOCol = 128;
@@ -398,10 +399,13 @@ struct TcLayout {
   static constexpr int kRingOff = kQBytes;
   static constexpr int kPOff = kRingOff + kTcStages * kStage;  // P head, then remainder
   static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  static constexpr int kNumBars = 2 * kTcStages + 5;  // kv_full, kv_empty, s_full x2, p_full, o_done, fin
+  // kv_full, kv_empty, s_full x2, p_full, o_done, fin, xchg x4 (one per lane quarter)
+  static constexpr int kNumBars = 2 * kTcStages + 9;
   static constexpr int kMaskOff = kBarOff + kNumBars * 8;
   static constexpr int kTmemOff = kMaskOff + kTcStages * 4;
-  static constexpr int kBytes = kTmemOff + 16;
+  static constexpr int kXmaxOff = kTmemOff + 16;               // float [2 stages][2 halves][128 rows]
+  static constexpr int kXlOff = kXmaxOff + 2 * 2 * kTcRows * 4;  // float [2 halves][128 rows]
+  static constexpr int kBytes = kXlOff + 2 * kTcRows * 4;
   static constexpr int kAlloc = kBytes + 1024;
 };
 
@@ -447,6 +451,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 1;
   uint64_t* fin = o_done + 1;
+  uint64_t* xchg = fin + 1;  // four: the two warps of a lane quarter swap row maxima
+  float* xmax = reinterpret_cast<float*>(smem + L::kXmaxOff);
+  float* xl = reinterpret_cast<float*>(smem + L::kXlOff);
   int* vmask = reinterpret_cast<int*>(smem + L::kMaskOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemOff);
   const uint32_t q_base = smem_addr(smem);
@@ -461,9 +468,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     mbar_init(smem_addr(&s_full[0]), 1);
     mbar_init(smem_addr(&s_full[1]), 1);
-    mbar_init(smem_addr(p_full), 4 * 32);
+    mbar_init(smem_addr(p_full), kTcSoftmaxWarps * 32);
     mbar_init(smem_addr(o_done), 1);
     mbar_init(smem_addr(fin), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&xchg[i]), 64);
     fence_mbar_init();
   }
   if (warp == kTcMmaWarp) {
@@ -610,12 +618,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax warps: thread = row ----------------
-    const int r = 32 * warp + lane;
+    // ---------------- softmax warps ----------------
+    // Warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (its rows) and the
+    // half w / 4 of each stage's 64 keys; the two warps of a lane quarter
+    // swap their row maxima through shared memory every stage (bounded
+    // mbarrier wait), so both apply the same running max, and split the O
+    // columns for the rescale and the epilogue.
+    constexpr int kHalf = kTcStageKeys / 2;
+    const int quad = warp & 3, half = warp >> 2;
+    const int r = 32 * quad + lane;
     const int t = r / G, h = r - t * G;
     const bool act = (t < ntok) && (r < a.tokens_per_tile * G);
     const int qpos = act ? pos0 + t : -1;
-    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(32 * quad) << 16);
+    const uint32_t xb = smem_addr(&xchg[quad]);
+    constexpr int kOChunks = D / 64;  // 32-column chunks of O per half
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int st = 0; st < nstages; ++st) {
@@ -627,23 +644,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[kTcStageKeys];
-      {
-        float(&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
-        float(&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
-        tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys), s0);
-        tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys + 32), s1);
-        tmem_wait_ld();
-      }
-      const int mask = vmask[slot];
-      const int key0 = st * kTcStageKeys;
+      float s[kHalf];
+      tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys + kHalf * half), s);
+      tmem_wait_ld();
+      const int mask = vmask[slot] >> (2 * half);  // bits of this half's two blocks
+      const int key0 = st * kTcStageKeys + kHalf * half;
+      // Stages wholly below every row's diagonal, with both blocks valid, need
+      // no mask: the max is taken on the raw scores and the scale is folded
+      // into the exponent (one FFMA per score).
+      const bool unmasked = __all_sync(0xffffffffu, (mask & 3) == 3 && key0 + kHalf - 1 <= qpos);
       float mx = -INFINITY;
+      if (unmasked) {
 #pragma unroll
-      for (int j = 0; j < kTcStageKeys; ++j) {
-        const bool valid = ((mask >> (j >> 4)) & 1) && (key0 + j <= qpos);
-        s[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[j]);
+        for (int j = 0; j < kHalf; ++j) mx = fmaxf(mx, s[j]);
+        mx *= a.scale_log2;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) {
+          const bool valid = ((mask >> (j >> 4)) & 1) && (key0 + j <= qpos);
+          s[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[j]);
+        }
       }
+      // both halves' maxima (buffers alternate by stage parity)
+      xmax[((st & 1) * 2 + half) * kTcRows + r] = mx;
+      mbar_arrive(xb);
+      const bool r5 = mbar_wait_bounded(xb, (uint32_t)st & 1u);
+      if (!__all_sync(0xffffffffu, r5)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, xmax[((st & 1) * 2 + (half ^ 1)) * kTcRows + r]);
       float alpha = 1.f;
       if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleLog2)) {
         alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
@@ -651,10 +682,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
       float ps = 0.f;
+      if (unmasked) {
 #pragma unroll
-      for (int j = 0; j < kTcStageKeys; ++j) {
-        s[j] = exp2f(s[j] - mu);
-        ps += s[j];
+        for (int j = 0; j < kHalf; ++j) {
+          s[j] = ex2_approx(fmaf(s[j], a.scale_log2, -mu));
+          ps += s[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) {
+          s[j] = ex2_approx(s[j] - mu);
+          ps += s[j];
+        }
       }
       l_run = l_run * alpha + ps;
       if (st > 0) {
@@ -667,41 +706,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < kOChunks; ++c) {
+            const uint32_t col = kTcOCol + (uint32_t)((half * kOChunks + c) * 32);
             float o[32];
-            tmem_ld32(trow + kTcOCol + c * 32, o);
+            tmem_ld32(trow + col, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(trow + kTcOCol + c * 32, o);
+            tmem_st32(trow + col, o);
           }
           tmem_wait_st();
         }
       }
-      // P (16-bit head and remainder) as two K-major A operands.
+      // P (16-bit head and remainder) as two K-major A operands; this half
+      // writes 16-byte chunks 4 half .. 4 half + 3 of its row.
 #pragma unroll
-      for (int c = 0; c < kTcStageKeys / 8; ++c) {
+      for (int c = 0; c < kHalf / 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) split2<T>(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
-        uint8_t* dst = smem + L::kPOff + r * 128 + ((c ^ (r & 7)) << 4);
+        const int cg = 4 * half + c;
+        uint8_t* dst = smem + L::kPOff + r * 128 + ((cg ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         *reinterpret_cast<uint4*>(dst + L::kPBytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       // V rows the MMA must not multiply (not loaded this stage, past the
       // context, or of a rejected block) are cleared: 0 * NaN would not be 0.
       {
-        const int keys_loaded = min(kTcStageKeys, nblk * kPBlock - key0);
-        const int keys_ctx = min(kTcStageKeys, ctx - key0);
+        const int smask = vmask[slot];
+        const int skey0 = st * kTcStageKeys;
+        const int keys_loaded = min(kTcStageKeys, nblk * kPBlock - skey0);
+        const int keys_ctx = min(kTcStageKeys, ctx - skey0);
         const int keep = min(keys_loaded, keys_ctx);
         const int full_mask = (1 << min(kStageBlocks, nblk - st * kStageBlocks)) - 1;
-        if (keep < kTcStageKeys || mask != full_mask) {
+        if (keep < kTcStageKeys || smask != full_mask) {
           uint8_t* vst = smem + L::kRingOff + (size_t)slot * L::kStage + L::kKBytes;
-          for (int i = threadIdx.x; i < kTcStageKeys * L::kBoxes * 8; i += 4 * 32) {
+          for (int i = threadIdx.x; i < kTcStageKeys * L::kBoxes * 8; i += kTcSoftmaxWarps * 32) {
             const int key = i / (L::kBoxes * 8);
             const int rem = i - key * (L::kBoxes * 8);
             const int b = rem >> 3, c = rem & 7;
-            const bool bad = key >= keep || !((mask >> (key >> 4)) & 1);
+            const bool bad = key >= keep || !((smask >> (key >> 4)) & 1);
             if (bad)
               *reinterpret_cast<uint4*>(vst + b * L::kKVBox + key * 128 + (c << 4)) = make_uint4(0, 0, 0, 0);
           }
@@ -713,21 +757,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (ok) {
       const bool r4 = mbar_wait_bounded(smem_addr(o_done), (uint32_t)(nstages - 1) & 1u);
-      if (__all_sync(0xffffffffu, r4)) {
+      // the row's exp-sum is the two halves' sums
+      xl[half * kTcRows + r] = l_run;
+      mbar_arrive(xb);
+      const bool r6 = mbar_wait_bounded(xb, (uint32_t)nstages & 1u);
+      if (__all_sync(0xffffffffu, r4 && r6)) {
         tc_fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const float l_tot = l_run + xl[(half ^ 1) * kTcRows + r];
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
         T* out = reinterpret_cast<T*>(a.out) +
                  (((size_t)q0 + tok0 + (act ? t : 0)) * a.num_heads + (size_t)kvh * G + h) * D;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kOChunks; ++c) {
+          const int cc = half * kOChunks + c;
           float o[32];
-          tmem_ld32(trow + kTcOCol + c * 32, o);
+          tmem_ld32(trow + kTcOCol + (uint32_t)(cc * 32), o);
           tmem_wait_ld();
           if (act) {
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = pack2<T>(o[2 * i] * inv, o[2 * i + 1] * inv);
-            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+            uint4* dst = reinterpret_cast<uint4*>(out + cc * 32);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
             dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
             dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
