@@ -358,55 +358,63 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 
 // ---------------------------------------------------------------------------
 // The same operator on 5th-generation tensor cores (tcgen05).  One CTA owns
-// 128 query rows (the M of every MMA) and 6 warps:
-//   warps 0-3  softmax and epilogue: thread = row, tensor-memory lane = row;
-//   warp 4     TMA producer (64-key stages of K and V, 3-stage ring);
-//   warp 5     tensor-memory owner and MMA issuer (one thread).
-// Tensor memory (256 columns): S double-buffered at columns [0,64) and
-// [64,128), the O accumulator at [128, 128 + D).
-// Per stage: S = Q K^T (M 128, N 64, K = D; Q and K as K-major operands in
-// 128-byte-swizzled shared memory), the softmax warps read S, mask, update
-// the running max / sum and write P (16-bit head and remainder, two K-major
-// A operands), then O += P_hi V + P_lo V (V as an MN-major B operand).  O is
+// two tiles of 128 query rows (A: rows 0-127, B: rows 128-255; each the M of
+// its MMAs) that share every K/V stage, and 10 warps:
+//   warps 0-3  softmax + epilogue of tile A, warps 4-7 of tile B: thread =
+//              row = tensor-memory lane (warp w reads lanes 32 (w % 4) ..);
+//   warp 8     TMA producer (64-key stages of K and V, 3-stage ring);
+//   warp 9     tensor-memory owner and MMA issuer (one thread).
+// Tensor memory (512 columns): tile A's S at [0, 64) and O at [64, 64 + D),
+// tile B's at [256, 320) and [320, 320 + D).
+// Per stage and tile: S = Q K^T (M 128, N 64, K = D; Q and K K-major in
+// 128-byte-swizzled shared memory); the tile's softmax warps read S, mask,
+// update the running max / sum and write P (16-bit head and remainder, two
+// K-major A operands); then O += P_hi V + P_lo V (V an MN-major B operand).
+// The MMA warp alternates the tiles -- PV_A(s), QK_A(s+1), PV_B(s),
+// QK_B(s+1) -- so one tile's softmax runs while the tensor core works for
+// the other, and every K/V byte brought in feeds 256 query rows.  O is
 // rescaled (tcgen05.ld / st) only when a row's max grows by more than 2^8:
 // until then P may exceed 1 by at most 2^8, which f32 accumulation absorbs.
-// K and V tiles are placed box-major ([64-column box][4 blocks][16 rows][128 B])
-// so one descriptor spans the 64 keys of a stage with an 8-row stride of
-// 1024 bytes.  Completion: tcgen05.commit -> mbarriers; all waits bounded.
+// K and V tiles are placed box-major ([64-column box][4 blocks][16 rows]
+// [128 B]) so one descriptor spans the 64 keys of a stage with an 8-row
+// stride of 1024 bytes.  Completion: tcgen05.commit -> mbarriers; every wait
+// is bounded.
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr int kTcRows = 128;
-constexpr int kTcSoftmaxWarps = 8;  // two per 32-row lane quarter: one per half of a stage's keys
+constexpr int kTcRows = 128;                 // rows of one tile (the MMA M)
+constexpr int kTcTiles = 2;
+constexpr int kTcCtaRows = kTcTiles * kTcRows;
+constexpr int kTcSoftmaxWarps = kTcTiles * 4;
 constexpr int kTcThreads = (kTcSoftmaxWarps + 2) * 32;
-constexpr int kTcProducerWarp = 8;
-constexpr int kTcMmaWarp = 9;
-constexpr int kTcStages = 4;
+constexpr int kTcProducerWarp = kTcSoftmaxWarps;
+constexpr int kTcMmaWarp = kTcSoftmaxWarps + 1;
+constexpr int kTcStages = 3;
 constexpr int kTcStageKeys = kStageBlocks * kPBlock;  // 64
-constexpr uint32_t kTcTmemCols = 256;
-constexpr uint32_t kTcOCol = 128;
+constexpr uint32_t kTcTmemCols = 512;
+constexpr uint32_t kTcTileCols = 256;  // tensor-memory columns of one tile
+constexpr uint32_t kTcOCol = 64;       // O after S within a tile's columns
 constexpr float kRescaleLog2 = 8.f;
 
 template <int D>
 struct TcLayout {
   static constexpr int kBoxes = D / 64;
   static constexpr int kQBox = kTcRows * 128;         // 16 KB: 128 rows x 128 B
-  static constexpr int kQBytes = kBoxes * kQBox;
+  static constexpr int kQBytes = kBoxes * kQBox;      // one tile's Q
   static constexpr int kKVBox = kTcStageKeys * 128;   // 8 KB: 64 keys x 128 B
   static constexpr int kKBytes = kBoxes * kKVBox;
   static constexpr int kStage = 2 * kKBytes;          // K, then V
   static constexpr int kPBytes = kTcRows * 128;       // 128 rows x 64 keys x 2 B
-  static constexpr int kRingOff = kQBytes;
-  static constexpr int kPOff = kRingOff + kTcStages * kStage;  // P head, then remainder
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  // kv_full, kv_empty, s_full x2, p_full, o_done, fin, xchg x4 (one per lane quarter)
-  static constexpr int kNumBars = 2 * kTcStages + 9;
+  static constexpr int kRingOff = kTcTiles * kQBytes;
+  static constexpr int kPOff = kRingOff + kTcStages * kStage;  // per tile: P head, then remainder
+  static constexpr int kBarOff = kPOff + kTcTiles * 2 * kPBytes;
+  // kv_full, kv_empty per stage; s_full, p_full, o_done per tile; fin
+  static constexpr int kNumBars = 2 * kTcStages + 3 * kTcTiles + 1;
   static constexpr int kMaskOff = kBarOff + kNumBars * 8;
   static constexpr int kTmemOff = kMaskOff + kTcStages * 4;
-  static constexpr int kXmaxOff = kTmemOff + 16;               // float [2 stages][2 halves][128 rows]
-  static constexpr int kXlOff = kXmaxOff + 2 * 2 * kTcRows * 4;  // float [2 halves][128 rows]
-  static constexpr int kBytes = kXlOff + 2 * kTcRows * 4;
+  static constexpr int kBytes = kTmemOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kAlloc <= 227 * 1024, "shared memory of one CTA");
 };
 
 }  // namespace
@@ -447,17 +455,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + kTcStages;
-  uint64_t* s_full = bars + 2 * kTcStages;  // two
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* fin = o_done + 1;
-  uint64_t* xchg = fin + 1;  // four: the two warps of a lane quarter swap row maxima
-  float* xmax = reinterpret_cast<float*>(smem + L::kXmaxOff);
-  float* xl = reinterpret_cast<float*>(smem + L::kXlOff);
+  uint64_t* s_full = bars + 2 * kTcStages;  // per tile
+  uint64_t* p_full = s_full + kTcTiles;     // per tile
+  uint64_t* o_done = p_full + kTcTiles;     // per tile
+  uint64_t* fin = o_done + kTcTiles;
   int* vmask = reinterpret_cast<int*>(smem + L::kMaskOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemOff);
-  const uint32_t q_base = smem_addr(smem);
-  const uint32_t p_base = smem_addr(smem + L::kPOff);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -466,32 +469,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(smem_addr(&kv_full[s]), 1);
       mbar_init(smem_addr(&kv_empty[s]), 1);
     }
-    mbar_init(smem_addr(&s_full[0]), 1);
-    mbar_init(smem_addr(&s_full[1]), 1);
-    mbar_init(smem_addr(p_full), kTcSoftmaxWarps * 32);
-    mbar_init(smem_addr(o_done), 1);
+    for (int x = 0; x < kTcTiles; ++x) {
+      mbar_init(smem_addr(&s_full[x]), 1);
+      mbar_init(smem_addr(&p_full[x]), 4 * 32);
+      mbar_init(smem_addr(&o_done[x]), 1);
+    }
     mbar_init(smem_addr(fin), 1);
-    for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&xchg[i]), 64);
     fence_mbar_init();
   }
   if (warp == kTcMmaWarp) {
     tmem_alloc(smem_addr(tmem_slot), kTcTmemCols);
     tmem_relinquish();
   }
-  // Q tile -> shared memory, K-major with the 128-byte swizzle: row r,
-  // 16-byte chunk c of its D elements at box c/8, line r, chunk (c%8)^(r%8).
+  // Q tiles -> shared memory, K-major with the 128-byte swizzle: row r of a
+  // tile, 16-byte chunk c of its D elements at box c/8, line r, chunk
+  // (c%8)^(r%8).  CTA row R = token R / G, head R % G.
   {
     constexpr int kChunks = D / 8;
-    for (int i = threadIdx.x; i < kTcRows * kChunks; i += kTcThreads) {
-      const int r = i / kChunks, c = i - (i / kChunks) * kChunks;
-      const int t = r / G, h = r - t * G;
-      const bool act = (t < ntok) && (r < a.tokens_per_tile * G);
+    for (int i = threadIdx.x; i < kTcCtaRows * kChunks; i += kTcThreads) {
+      const int R = i / kChunks, c = i - (i / kChunks) * kChunks;
+      const int t = R / G, h = R - t * G;
+      const bool act = (t < ntok) && (R < a.tokens_per_tile * G);
       uint4 v = make_uint4(0, 0, 0, 0);
       if (act)
         v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.q) +
                                             (((size_t)q0 + tok0 + t) * a.num_heads + (size_t)kvh * G + h) * D +
                                             c * 8);
-      *reinterpret_cast<uint4*>(smem + (c >> 3) * L::kQBox + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      const int x = R / kTcRows, r = R - x * kTcRows;
+      *reinterpret_cast<uint4*>(smem + x * L::kQBytes + (c >> 3) * L::kQBox + r * 128 +
+                                (((c & 7) ^ (r & 7)) << 4)) = v;
     }
   }
   fence_proxy_async_smem();
@@ -565,51 +571,67 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
-      auto issue_qk = [&](int st) {
+      const uint32_t q_base = smem_addr(smem);
+      const uint32_t p_base = smem_addr(smem + L::kPOff);
+      auto issue_qk = [&](int st, int x) {
         const uint32_t kb = smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage);
-        const uint32_t d = tmem + (uint32_t)((st & 1) * kTcStageKeys);
+        const uint32_t qb = q_base + x * L::kQBytes;
+        const uint32_t d = tmem + x * kTcTileCols;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(q_base + (kk >> 2) * L::kQBox + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = smem_desc_sw128(qb + (kk >> 2) * L::kQBox + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(kb + (kk >> 2) * L::kKVBox + (kk & 3) * 32, 16, 1024);
           tc_mma_f16(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        tc_commit(smem_addr(&s_full[st & 1]));
+        tc_commit(smem_addr(&s_full[x]));
       };
-      if (mbar_wait_bounded(smem_addr(&kv_full[0]), 0)) {
-        tc_fence_after();
-        issue_qk(0);
-      } else {
-        ok = false;
-      }
-      for (int st = 0; ok && st < nstages; ++st) {
-        if (st + 1 < nstages) {
-          if (!mbar_wait_bounded(smem_addr(&kv_full[(st + 1) % kTcStages]),
-                                 (uint32_t)((st + 1) / kTcStages) & 1u)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_qk(st + 1);
-        }
-        if (!mbar_wait_bounded(smem_addr(p_full), (uint32_t)st & 1u)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      auto issue_pv = [&](int st, int x) {
         const uint32_t vb =
             smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage + L::kKBytes);
+        const uint32_t pb = p_base + x * 2 * L::kPBytes;
+        const uint32_t d = tmem + x * kTcTileCols + kTcOCol;
 #pragma unroll
         for (int j = 0; j < kStageBlocks; ++j) {
 #pragma unroll
           for (int hl = 0; hl < 2; ++hl) {
-            const uint64_t ad = smem_desc_sw128(p_base + hl * L::kPBytes + j * 32, 16, 1024);
+            const uint64_t ad = smem_desc_sw128(pb + hl * L::kPBytes + j * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(vb + j * kBoxBytes, L::kKVBox, 1024);
-            tc_mma_f16(tmem + kTcOCol, ad, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
+            tc_mma_f16(d, ad, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
           }
         }
-        tc_commit(smem_addr(o_done));
-        tc_commit(smem_addr(&kv_empty[st % kTcStages]));
+        tc_commit(smem_addr(&o_done[x]));
+      };
+      if (mbar_wait_bounded(smem_addr(&kv_full[0]), 0)) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(0, 1);
+      } else {
+        ok = false;
+      }
+      for (int st = 0; ok && st < nstages; ++st) {
+        const bool next = st + 1 < nstages;
+        for (int x = 0; x < kTcTiles; ++x) {
+          // P of this tile written (and its S read): PV, then the next S.
+          if (!mbar_wait_bounded(smem_addr(&p_full[x]), (uint32_t)st & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(st, x);
+          // after the last tile's PV this stage's K/V may be refilled
+          if (x == kTcTiles - 1) tc_commit(smem_addr(&kv_empty[st % kTcStages]));
+          if (next) {
+            if (x == 0) {
+              if (!mbar_wait_bounded(smem_addr(&kv_full[(st + 1) % kTcStages]),
+                                     (uint32_t)((st + 1) / kTcStages) & 1u)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            issue_qk(st + 1, x);
+          }
+        }
       }
       if (!ok) prefill_error(CF_DEVERR_TIMEOUT);
       // Every MMA issued above has finished before tensor memory is released.
@@ -618,63 +640,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax warps ----------------
-    // Warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (its rows) and the
-    // half w / 4 of each stage's 64 keys; the two warps of a lane quarter
-    // swap their row maxima through shared memory every stage (bounded
-    // mbarrier wait), so both apply the same running max, and split the O
-    // columns for the rescale and the epilogue.
-    constexpr int kHalf = kTcStageKeys / 2;
-    const int quad = warp & 3, half = warp >> 2;
-    const int r = 32 * quad + lane;
-    const int t = r / G, h = r - t * G;
-    const bool act = (t < ntok) && (r < a.tokens_per_tile * G);
+    // ---------------- softmax warps of tile x: thread = row ----------------
+    const int x = warp >> 2, quad = warp & 3;
+    const int r = 32 * quad + lane;  // row within the tile = tensor-memory lane
+    const int R = x * kTcRows + r;   // row within the CTA
+    const int t = R / G, h = R - t * G;
+    const bool act = (t < ntok) && (R < a.tokens_per_tile * G);
     const int qpos = act ? pos0 + t : -1;
-    const uint32_t trow = tmem + ((uint32_t)(32 * quad) << 16);
-    const uint32_t xb = smem_addr(&xchg[quad]);
-    constexpr int kOChunks = D / 64;  // 32-column chunks of O per half
+    const uint32_t trow = tmem + ((uint32_t)(32 * quad) << 16) + x * kTcTileCols;
+    uint8_t* const prow = smem + L::kPOff + x * 2 * L::kPBytes + r * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int st = 0; st < nstages; ++st) {
       const int slot = st % kTcStages;
-      const bool r1 = mbar_wait_bounded(smem_addr(&s_full[st & 1]), (uint32_t)(st >> 1) & 1u);
+      const bool r1 = mbar_wait_bounded(smem_addr(&s_full[x]), (uint32_t)st & 1u);
       const bool r2 = mbar_wait_bounded(smem_addr(&kv_full[slot]), (uint32_t)(st / kTcStages) & 1u);
       if (!__all_sync(0xffffffffu, r1 && r2)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kHalf];
-      tmem_ld32(trow + (uint32_t)((st & 1) * kTcStageKeys + kHalf * half), s);
-      tmem_wait_ld();
-      const int mask = vmask[slot] >> (2 * half);  // bits of this half's two blocks
-      const int key0 = st * kTcStageKeys + kHalf * half;
-      // Stages wholly below every row's diagonal, with both blocks valid, need
+      float s[kTcStageKeys];
+      {
+        float(&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
+        float(&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
+        tmem_ld32(trow, s0);
+        tmem_ld32(trow + 32, s1);
+        tmem_wait_ld();
+      }
+      const int mask = vmask[slot];
+      const int key0 = st * kTcStageKeys;
+      // Stages wholly below every row's diagonal, with all blocks valid, need
       // no mask: the max is taken on the raw scores and the scale is folded
       // into the exponent (one FFMA per score).
-      const bool unmasked = __all_sync(0xffffffffu, (mask & 3) == 3 && key0 + kHalf - 1 <= qpos);
+      const bool unmasked = __all_sync(0xffffffffu, mask == 15 && key0 + kTcStageKeys - 1 <= qpos);
       float mx = -INFINITY;
       if (unmasked) {
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) mx = fmaxf(mx, s[j]);
+        for (int j = 0; j < kTcStageKeys; ++j) mx = fmaxf(mx, s[j]);
         mx *= a.scale_log2;
       } else {
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) {
+        for (int j = 0; j < kTcStageKeys; ++j) {
           const bool valid = ((mask >> (j >> 4)) & 1) && (key0 + j <= qpos);
           s[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
           mx = fmaxf(mx, s[j]);
         }
       }
-      // both halves' maxima (buffers alternate by stage parity)
-      xmax[((st & 1) * 2 + half) * kTcRows + r] = mx;
-      mbar_arrive(xb);
-      const bool r5 = mbar_wait_bounded(xb, (uint32_t)st & 1u);
-      if (!__all_sync(0xffffffffu, r5)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, xmax[((st & 1) * 2 + (half ^ 1)) * kTcRows + r]);
       float alpha = 1.f;
       if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleLog2)) {
         alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
@@ -684,21 +696,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float ps = 0.f;
       if (unmasked) {
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) {
+        for (int j = 0; j < kTcStageKeys; ++j) {
           s[j] = ex2_approx(fmaf(s[j], a.scale_log2, -mu));
           ps += s[j];
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) {
+        for (int j = 0; j < kTcStageKeys; ++j) {
           s[j] = ex2_approx(s[j] - mu);
           ps += s[j];
         }
       }
       l_run = l_run * alpha + ps;
       if (st > 0) {
-        // PV of the previous stage reads P and writes O: wait for it.
-        const bool r3 = mbar_wait_bounded(smem_addr(o_done), (uint32_t)(st - 1) & 1u);
+        // This tile's previous PV reads P and writes O: wait for it.
+        const bool r3 = mbar_wait_bounded(smem_addr(&o_done[x]), (uint32_t)(st - 1) & 1u);
         if (!__all_sync(0xffffffffu, r3)) {
           ok = false;
           break;
@@ -706,46 +718,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < kOChunks; ++c) {
-            const uint32_t col = kTcOCol + (uint32_t)((half * kOChunks + c) * 32);
+          for (int c = 0; c < D / 32; ++c) {
             float o[32];
-            tmem_ld32(trow + col, o);
+            tmem_ld32(trow + kTcOCol + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(trow + col, o);
+            tmem_st32(trow + kTcOCol + c * 32, o);
           }
           tmem_wait_st();
         }
       }
-      // P (16-bit head and remainder) as two K-major A operands; this half
-      // writes 16-byte chunks 4 half .. 4 half + 3 of its row.
+      // P (16-bit head and remainder) as two K-major A operands.
 #pragma unroll
-      for (int c = 0; c < kHalf / 8; ++c) {
+      for (int c = 0; c < kTcStageKeys / 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) split2<T>(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
-        const int cg = 4 * half + c;
-        uint8_t* dst = smem + L::kPOff + r * 128 + ((cg ^ (r & 7)) << 4);
+        uint8_t* dst = prow + ((c ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         *reinterpret_cast<uint4*>(dst + L::kPBytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       // V rows the MMA must not multiply (not loaded this stage, past the
-      // context, or of a rejected block) are cleared: 0 * NaN would not be 0.
-      {
-        const int smask = vmask[slot];
-        const int skey0 = st * kTcStageKeys;
-        const int keys_loaded = min(kTcStageKeys, nblk * kPBlock - skey0);
-        const int keys_ctx = min(kTcStageKeys, ctx - skey0);
+      // context, or of a rejected block) are cleared by tile A's warps before
+      // they release tile A's P (tile B's PV follows tile A's): 0 * NaN would
+      // not be 0.
+      if (x == 0) {
+        const int keys_loaded = min(kTcStageKeys, nblk * kPBlock - key0);
+        const int keys_ctx = min(kTcStageKeys, ctx - key0);
         const int keep = min(keys_loaded, keys_ctx);
         const int full_mask = (1 << min(kStageBlocks, nblk - st * kStageBlocks)) - 1;
-        if (keep < kTcStageKeys || smask != full_mask) {
+        if (keep < kTcStageKeys || mask != full_mask) {
           uint8_t* vst = smem + L::kRingOff + (size_t)slot * L::kStage + L::kKBytes;
-          for (int i = threadIdx.x; i < kTcStageKeys * L::kBoxes * 8; i += kTcSoftmaxWarps * 32) {
+          for (int i = threadIdx.x; i < kTcStageKeys * L::kBoxes * 8; i += 4 * 32) {
             const int key = i / (L::kBoxes * 8);
             const int rem = i - key * (L::kBoxes * 8);
             const int b = rem >> 3, c = rem & 7;
-            const bool bad = key >= keep || !((smask >> (key >> 4)) & 1);
+            const bool bad = key >= keep || !((mask >> (key >> 4)) & 1);
             if (bad)
               *reinterpret_cast<uint4*>(vst + b * L::kKVBox + key * 128 + (c << 4)) = make_uint4(0, 0, 0, 0);
           }
@@ -753,31 +762,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(smem_addr(p_full));
+      mbar_arrive(smem_addr(&p_full[x]));
     }
     if (ok) {
-      const bool r4 = mbar_wait_bounded(smem_addr(o_done), (uint32_t)(nstages - 1) & 1u);
-      // the row's exp-sum is the two halves' sums
-      xl[half * kTcRows + r] = l_run;
-      mbar_arrive(xb);
-      const bool r6 = mbar_wait_bounded(xb, (uint32_t)nstages & 1u);
-      if (__all_sync(0xffffffffu, r4 && r6)) {
+      const bool r4 = mbar_wait_bounded(smem_addr(&o_done[x]), (uint32_t)(nstages - 1) & 1u);
+      if (__all_sync(0xffffffffu, r4)) {
         tc_fence_after();
-        const float l_tot = l_run + xl[(half ^ 1) * kTcRows + r];
-        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         T* out = reinterpret_cast<T*>(a.out) +
                  (((size_t)q0 + tok0 + (act ? t : 0)) * a.num_heads + (size_t)kvh * G + h) * D;
 #pragma unroll 1
-        for (int c = 0; c < kOChunks; ++c) {
-          const int cc = half * kOChunks + c;
+        for (int c = 0; c < D / 32; ++c) {
           float o[32];
-          tmem_ld32(trow + kTcOCol + (uint32_t)(cc * 32), o);
+          tmem_ld32(trow + kTcOCol + c * 32, o);
           tmem_wait_ld();
           if (act) {
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = pack2<T>(o[2 * i] * inv, o[2 * i + 1] * inv);
-            uint4* dst = reinterpret_cast<uint4*>(out + cc * 32);
+            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
             dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
             dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
@@ -843,7 +846,7 @@ cf_status launch_prefill_typed(const cf_prefill_params& p, bool tcgen05, cudaStr
     static cudaError_t errs[64];
     cf_status s = ensure_prefill_smem(paged_prefill_tc_kernel<T, D>, TcLayout<D>::kAlloc, flags, errs);
     if (s != CF_OK) return s;
-    const PrefillArgs a = make_args(p, kTcRows);
+    const PrefillArgs a = make_args(p, kTcCtaRows);
     const int tiles = (p.max_query_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
     dim3 grid((unsigned)tiles, (unsigned)p.num_kv_heads, (unsigned)p.num_chunks);
     paged_prefill_tc_kernel<T, D><<<grid, kTcThreads, TcLayout<D>::kAlloc, stream>>>(a, tmk, tmv);
