@@ -364,12 +364,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 //              row = tensor-memory lane (warp w reads lanes 32 (w % 4) ..);
 //   warp 8     TMA producer (64-key stages of K and V, 3-stage ring);
 //   warp 9     tensor-memory owner and MMA issuer (one thread).
-// Tensor memory (512 columns): tile A's S at [0, 64) and O at [64, 64 + D),
-// tile B's at [256, 320) and [320, 320 + D).
+// Tensor memory (512 columns), per tile: S double-buffered at [0, 64) and
+// [64, 128), O at [128, 128 + D); tile B at +256.
 // Per stage and tile: S = Q K^T (M 128, N 64, K = D; Q and K K-major in
 // 128-byte-swizzled shared memory); the tile's softmax warps read S, mask,
-// update the running max / sum and write P (16-bit head and remainder, two
-// K-major A operands); then O += P_hi V + P_lo V (V an MN-major B operand).
+// update the running max / sum and write P over the S buffer it came from
+// (16-bit head in its first 32 columns, remainder in the next 32: K-major A
+// operands in tensor memory); then O += P_hi V + P_lo V with A read from
+// tensor memory and V an MN-major B operand in shared memory.
 // The MMA warp alternates the tiles -- PV_A(s), QK_A(s+1), PV_B(s),
 // QK_B(s+1) -- so one tile's softmax runs while the tensor core works for
 // the other, and every K/V byte brought in feeds 256 query rows.  O is
@@ -389,11 +391,12 @@ constexpr int kTcSoftmaxWarps = kTcTiles * 4;
 constexpr int kTcThreads = (kTcSoftmaxWarps + 2) * 32;
 constexpr int kTcProducerWarp = kTcSoftmaxWarps;
 constexpr int kTcMmaWarp = kTcSoftmaxWarps + 1;
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 5;
 constexpr int kTcStageKeys = kStageBlocks * kPBlock;  // 64
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcTileCols = 256;  // tensor-memory columns of one tile
-constexpr uint32_t kTcOCol = 64;       // O after S within a tile's columns
+constexpr uint32_t kTcSCols = 64;      // one S buffer (later P head + remainder)
+constexpr uint32_t kTcOCol = 128;      // O after the two S buffers
 constexpr float kRescaleLog2 = 8.f;
 
 template <int D>
@@ -404,10 +407,8 @@ struct TcLayout {
   static constexpr int kKVBox = kTcStageKeys * 128;   // 8 KB: 64 keys x 128 B
   static constexpr int kKBytes = kBoxes * kKVBox;
   static constexpr int kStage = 2 * kKBytes;          // K, then V
-  static constexpr int kPBytes = kTcRows * 128;       // 128 rows x 64 keys x 2 B
   static constexpr int kRingOff = kTcTiles * kQBytes;
-  static constexpr int kPOff = kRingOff + kTcStages * kStage;  // per tile: P head, then remainder
-  static constexpr int kBarOff = kPOff + kTcTiles * 2 * kPBytes;
+  static constexpr int kBarOff = kRingOff + kTcStages * kStage;
   // kv_full, kv_empty per stage; s_full, p_full, o_done per tile; fin
   static constexpr int kNumBars = 2 * kTcStages + 3 * kTcTiles + 1;
   static constexpr int kMaskOff = kBarOff + kNumBars * 8;
@@ -572,11 +573,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       bool ok = true;
       const uint32_t q_base = smem_addr(smem);
-      const uint32_t p_base = smem_addr(smem + L::kPOff);
       auto issue_qk = [&](int st, int x) {
         const uint32_t kb = smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage);
         const uint32_t qb = q_base + x * L::kQBytes;
-        const uint32_t d = tmem + x * kTcTileCols;
+        const uint32_t d = tmem + x * kTcTileCols + (st & 1) * kTcSCols;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t ad = smem_desc_sw128(qb + (kk >> 2) * L::kQBox + (kk & 3) * 32, 16, 1024);
@@ -588,15 +588,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       auto issue_pv = [&](int st, int x) {
         const uint32_t vb =
             smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage + L::kKBytes);
-        const uint32_t pb = p_base + x * 2 * L::kPBytes;
+        const uint32_t pt = tmem + x * kTcTileCols + (st & 1) * kTcSCols;  // P of this stage
         const uint32_t d = tmem + x * kTcTileCols + kTcOCol;
 #pragma unroll
         for (int j = 0; j < kStageBlocks; ++j) {
 #pragma unroll
           for (int hl = 0; hl < 2; ++hl) {
-            const uint64_t ad = smem_desc_sw128(pb + hl * L::kPBytes + j * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(vb + j * kBoxBytes, L::kKVBox, 1024);
-            tc_mma_f16(d, ad, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
+            tc_mma_f16_ts(d, pt + hl * (kTcSCols / 2) + j * 8, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
           }
         }
         tc_commit(smem_addr(&o_done[x]));
@@ -648,7 +647,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool act = (t < ntok) && (R < a.tokens_per_tile * G);
     const int qpos = act ? pos0 + t : -1;
     const uint32_t trow = tmem + ((uint32_t)(32 * quad) << 16) + x * kTcTileCols;
-    uint8_t* const prow = smem + L::kPOff + x * 2 * L::kPBytes + r * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int st = 0; st < nstages; ++st) {
@@ -664,8 +662,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       {
         float(&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
         float(&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
-        tmem_ld32(trow, s0);
-        tmem_ld32(trow + 32, s1);
+        tmem_ld32(trow + (st & 1) * kTcSCols, s0);
+        tmem_ld32(trow + (st & 1) * kTcSCols + 32, s1);
         tmem_wait_ld();
       }
       const int mask = vmask[slot];
@@ -709,7 +707,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       l_run = l_run * alpha + ps;
       if (st > 0) {
-        // This tile's previous PV reads P and writes O: wait for it.
+        // This tile's previous PV writes O (and read the other S buffer,
+        // which the next QK overwrites): wait for it.
         const bool r3 = mbar_wait_bounded(smem_addr(&o_done[x]), (uint32_t)(st - 1) & 1u);
         if (!__all_sync(0xffffffffu, r3)) {
           ok = false;
@@ -729,15 +728,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tmem_wait_st();
         }
       }
-      // P (16-bit head and remainder) as two K-major A operands.
+      // P (16-bit head and remainder) over this stage's S buffer: keys
+      // 2c, 2c+1 in column c (head) and column 32 + c (remainder).
+      {
+        uint32_t hi[kTcStageKeys / 2], lo[kTcStageKeys / 2];
 #pragma unroll
-      for (int c = 0; c < kTcStageKeys / 8; ++c) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) split2<T>(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
-        uint8_t* dst = prow + ((c ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(dst + L::kPBytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        for (int c = 0; c < kTcStageKeys / 2; ++c) split2<T>(s[2 * c], s[2 * c + 1], hi[c], lo[c]);
+        tmem_st32(trow + (st & 1) * kTcSCols, reinterpret_cast<float(&)[32]>(hi));
+        tmem_st32(trow + (st & 1) * kTcSCols + 32, reinterpret_cast<float(&)[32]>(lo));
+        tmem_wait_st();
       }
       // V rows the MMA must not multiply (not loaded this stage, past the
       // context, or of a rejected block) are cleared by tile A's warps before
@@ -758,9 +757,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (bad)
               *reinterpret_cast<uint4*>(vst + b * L::kKVBox + key * 128 + (c << 4)) = make_uint4(0, 0, 0, 0);
           }
+          fence_proxy_async_smem();  // the PV MMAs read these rows through the async proxy
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(smem_addr(&p_full[x]));
     }
