@@ -672,39 +672,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // no mask: the max is taken on the raw scores and the scale is folded
       // into the exponent (one FFMA per score).
       const bool unmasked = __all_sync(0xffffffffu, mask == 15 && key0 + kTcStageKeys - 1 <= qpos);
-      float mx = -INFINITY;
+      // Row max and row sum over 8 independent partials (no 64-long
+      // dependency chain).
+      float part[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) part[i] = -INFINITY;
       if (unmasked) {
 #pragma unroll
-        for (int j = 0; j < kTcStageKeys; ++j) mx = fmaxf(mx, s[j]);
-        mx *= a.scale_log2;
+        for (int j = 0; j < kTcStageKeys; ++j) part[j & 7] = fmaxf(part[j & 7], s[j]);
       } else {
 #pragma unroll
         for (int j = 0; j < kTcStageKeys; ++j) {
           const bool valid = ((mask >> (j >> 4)) & 1) && (key0 + j <= qpos);
           s[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[j]);
+          part[j & 7] = fmaxf(part[j & 7], s[j]);
         }
       }
+      float mx = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
+                       fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7])));
+      if (unmasked) mx *= a.scale_log2;
       float alpha = 1.f;
       if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleLog2)) {
         alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
         m_run = mx;
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-      float ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) part[i] = 0.f;
       if (unmasked) {
 #pragma unroll
         for (int j = 0; j < kTcStageKeys; ++j) {
           s[j] = ex2_approx(fmaf(s[j], a.scale_log2, -mu));
-          ps += s[j];
+          part[j & 7] += s[j];
         }
       } else {
 #pragma unroll
         for (int j = 0; j < kTcStageKeys; ++j) {
           s[j] = ex2_approx(s[j] - mu);
-          ps += s[j];
+          part[j & 7] += s[j];
         }
       }
+      const float ps = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
       l_run = l_run * alpha + ps;
       if (st > 0) {
         // This tile's previous PV writes O (and read the other S buffer,
