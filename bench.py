@@ -301,6 +301,11 @@ def run_ours(args):
     # batches that fit in L2 (126 MB) are timed with L2 overwritten between steps
     flush = (torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
              if w.kv_bytes() < 4 * L2_BYTES else None)
+    # After the write, a read of a second (clean) buffer leaves L2 holding
+    # clean lines only, so the timed step does not also pay for writing the
+    # flush buffer's dirty lines back to HBM (--l2-clean off keeps them).
+    flush_clean = (torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+                   if flush is not None and args.l2_clean == "on" else None)
 
     def step(record=False):
         if pairs is not None:
@@ -344,6 +349,8 @@ def run_ours(args):
                 # the batch fits in L2: overwrite L2 before every step and time
                 # the steps alone
                 flush.zero_()
+                if flush_clean is not None:
+                    flush_clean.max()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
                 step(record=True)
@@ -456,7 +463,9 @@ def run_ours(args):
                            else "reshape_and_cache launch before attention"),
                 "kv_dtype": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % kv_scale
                              if fp8 else w.dtype),
-                "l2": ("L2 flushed before every timed step (512 MB write, outside the step's events)"
+                "l2": (("L2 flushed before every timed step (512 MB write, then a 512 MB read of a clean buffer; "
+                        "outside the step's events)" if flush_clean is not None else
+                        "L2 flushed before every timed step (512 MB write, outside the step's events)")
                        if flush is not None else
                        "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (kv_step / 1e9)),
                 "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes() // (w.elem_bytes if fp8 else 1),
@@ -613,6 +622,8 @@ def main():
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--l2-clean", choices=["on", "off"], default="on",
+                    help="small batches: read a clean buffer after the L2-flush write")
     ap.add_argument("--kv-dtype", choices=["native", "fp8"], default="native",
                     help="KV cache element type: the workload's own, or fp8 e4m3 with a per-cache scale")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
