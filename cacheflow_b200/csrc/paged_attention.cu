@@ -441,27 +441,37 @@ struct MmaConsumerFp8 {
       }
     }
     float bm = -INFINITY;
+    if (ntok == kBlockTokens) {  // every block but a sequence's last
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int tok = nt * 8 + 2 * t + j;
-        const float x = s[nt][j] * scale_log2;
-        s[nt][j] = tok < ntok ? x : -INFINITY;
-        bm = fmaxf(bm, s[nt][j]);
-      }
+        for (int j = 0; j < 2; ++j) {
+          s[nt][j] *= scale_log2;
+          bm = fmaxf(bm, s[nt][j]);
+        }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int tok = nt * 8 + 2 * t + j;
+          const float x = s[nt][j] * scale_log2;
+          s[nt][j] = tok < ntok ? x : -INFINITY;
+          bm = fmaxf(bm, s[nt][j]);
+        }
+    }
     bm = fmaxf(bm, shfl_xor(bm, 1));
     bm = fmaxf(bm, shfl_xor(bm, 2));
     const float mn = fmaxf(m, bm);
     const float mu = (mn == -INFINITY) ? 0.f : mn;
-    const float alpha = exp2f(m - mu);
+    const float alpha = ex2_approx(m - mu);
     m = mn;
     float ps = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        s[nt][j] = exp2f(s[nt][j] - mu);
+        s[nt][j] = ex2_approx(s[nt][j] - mu);
         ps += s[nt][j];
       }
     l = l * alpha + ps;
