@@ -7,8 +7,12 @@
 // per sequence); a chunk of T tokens there is T decode rows with causal
 // context lengths, each re-reading the whole context.  Here one CTA takes a
 // tile of query tokens x the query heads of one KV head and streams the
-// context once for all of them:
+// context once for all of them.  Two kernels:
 //
+//   paged_prefill_tc_kernel (default): tcgen05 tensor cores with tensor-memory
+//   accumulators, two 128-row tiles per CTA; described above the kernel.
+//
+//   paged_prefill_kernel (CF_PREFILL_CONSUMER=mma): mma.sync, 64 rows per CTA:
 //   * 4 consumer warps own 16 query rows each (row = token * G + head within
 //     the GQA group G), Q held as mma.sync A fragments for the whole tile;
 //   * a producer warp streams 64-token stages (4 KV blocks of K and V) with
