@@ -488,7 +488,10 @@ def run_ours(args):
                 "peak_source": peak_kind,
                 "alg_bytes_per_launch": alg_bytes,
                 "kernel_ms": round(att_ms, 4),
-                "traffic": traffic_from_profiles(w.name + ("_fp8" if fp8 else "")),
+                # the committed captures are of 1-GPU launches: a strong-scaled
+                # rank's launch is another shape
+                "traffic": (traffic_from_profiles(w.name + ("_fp8" if fp8 else ""))
+                            if world == 1 or scaling == "weak" else None),
             },
             "e2e": {
                 "value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 1),
