@@ -1,6 +1,6 @@
-// cache_ops.cu -- KV-cache data movement for sm_100a: reshape_and_cache,
-// block-pair copies (copy_blocks, swap_blocks, compact_kv_cache) and
-// memset_blocks.
+// cache_ops.cu -- KV-cache data movement for sm_100a: reshape_and_cache (and
+// its fp8-quantizing form), block-pair copies (copy_blocks, swap_blocks,
+// compact_kv_cache), memset_blocks, and the device-side decode-input builder.
 //
 // All of these are pure byte movement and HBM-bound (or host-link-bound for
 // swaps), so the kernels move 16-byte vectors with 64-bit offsets, spread

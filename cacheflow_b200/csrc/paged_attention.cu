@@ -17,14 +17,20 @@
 //     so every KV byte is read from HBM once per KV head.
 //   * Each of the NW warps streams its own share of the partition's 16-token
 //     blocks through a private S-stage ring in shared memory.  Lane 0 of the
-//     warp issues 1-D bulk async copies (TMA, cp.async.bulk) of the 4 KB
-//     (bf16/fp16, D=128) K and V tiles of a block, completion tracked by one
-//     mbarrier per stage; the warp computes on stage i while stages i+1..i+S-1
-//     are in flight.  Block-table entries are fetched 32 at a time by the warp
-//     and broadcast with shuffles.
-//   * Per warp: online softmax in the log2 domain (q pre-scaled by
-//     scale*log2(e)), QK dot products by 8-lane groups with xor-shuffle
-//     reductions, PV with each lane owning D/32 output columns.
+//     warp issues the async copies of a block's K and V tiles (4 KB each for
+//     bf16/fp16 at D=128): 1-D bulk copies (cp.async.bulk) for the FMA
+//     consumer, 2-D tensor-map boxes with the 128-byte swizzle for the
+//     tensor-core consumers; completion is tracked by one mbarrier per stage,
+//     and the warp computes on stage i while stages i+1..i+S-1 are in flight.
+//     Block-table entries are fetched 32 at a time by the warp and broadcast
+//     with shuffles.
+//   * Consumers (per warp, online softmax in the log2 domain): FMA -- QK dot
+//     products by 8-lane groups with xor-shuffle reductions, PV with each lane
+//     owning D/32 output columns; MMA -- mma.sync for 16-bit caches with up to
+//     8 query heads as the rows; MmaConsumerFp8 -- the same for e4m3 caches,
+//     converted to f16 in registers.
+//   * Optional fused append: the newest token of each row is patched into its
+//     tile and written to the cache by the same launch.
 //   * Warps are merged through shared memory at the end of the partition.
 //     A sequence that fits one partition writes its output directly;
 //     otherwise the partition writes (max logit, exp-sum, normalised partial
