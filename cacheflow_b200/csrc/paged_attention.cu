@@ -92,7 +92,7 @@ struct AttnArgs {
 // shared-memory reads are conflict-free without swizzling), PV with lane l
 // owning columns [l*D/32, (l+1)*D/32).
 // ---------------------------------------------------------------------------
-template <typename T, typename TC, int D, int HG>
+template <typename T, typename TC, int D, int HG, int R>
 struct FmaConsumer {
   static constexpr int kVec = 16 / (int)sizeof(TC);          // cache elements per 16 B
   static constexpr int kChunks = D * (int)sizeof(TC) / 128;  // 16 B chunks per lane (QK)
@@ -131,23 +131,24 @@ struct FmaConsumer {
     load_widen<TC, kEpl>(vrow + t * D, vf);
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
-      const float pt = pt_h[h * kBlockTokens + t];
+      const float pt = pt_h[h * R + t];
 #pragma unroll
       for (int e = 0; e < kEpl; ++e) o[h][e] = fmaf(pt, vf[e], o[h][e]);
     }
   }
 
-  // One 16-token block; `ntok` valid tokens (1..16).  `pbuf` is this warp's
-  // HG*16-float scratch.
+  // One tile of R tokens (a 16-token block, or half of one); `ntok` valid
+  // tokens (1..R).  `pbuf` is this warp's HG*R-float scratch.
   __device__ __forceinline__ void block(const uint8_t* kraw, const uint8_t* vraw, int ntok,
                                         float* pbuf, int lane) {
+    constexpr int kPasses = R / 4;  // 4 tokens per pass (one per 8-lane group)
     const TC* kt = reinterpret_cast<const TC*>(kraw);
     const TC* vt = reinterpret_cast<const TC*>(vraw);
     const int j = lane >> 3;
     const int i = lane & 7;
-    float s[4][HG];
+    float s[kPasses][HG];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < kPasses; ++p) {
       const int tok = p * 4 + j;
       const TC* row = kt + tok * D;
       float acc[HG];
@@ -173,7 +174,9 @@ struct FmaConsumer {
     }
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
-      float bm = fmaxf(fmaxf(s[0][h], s[1][h]), fmaxf(s[2][h], s[3][h]));
+      float bm = s[0][h];
+#pragma unroll
+      for (int p = 1; p < kPasses; ++p) bm = fmaxf(bm, s[p][h]);
       bm = fmaxf(bm, shfl_xor(bm, 8));
       bm = fmaxf(bm, shfl_xor(bm, 16));
       const float mn = fmaxf(m[h], bm);
@@ -182,7 +185,7 @@ struct FmaConsumer {
       m[h] = mn;
       float ps = 0.f;
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < kPasses; ++p) {
         s[p][h] = exp2f(s[p][h] - mu);
         ps += s[p][h];
       }
@@ -193,14 +196,14 @@ struct FmaConsumer {
       for (int e = 0; e < kEpl; ++e) o[h][e] *= alpha;
       if (i == 0) {
 #pragma unroll
-        for (int p = 0; p < 4; ++p) pbuf[h * kBlockTokens + p * 4 + j] = s[p][h];
+        for (int p = 0; p < kPasses; ++p) pbuf[h * R + p * 4 + j] = s[p][h];
       }
     }
     __syncwarp();
     const TC* vrow = vt + lane * kEpl;
-    if (ntok == kBlockTokens) {
+    if (ntok == R) {
 #pragma unroll
-      for (int t = 0; t < kBlockTokens; ++t) pv_token(vrow, pbuf, t);
+      for (int t = 0; t < R; ++t) pv_token(vrow, pbuf, t);
     } else {
 #pragma unroll 1
       for (int t = 0; t < ntok; ++t) pv_token(vrow, pbuf, t);
@@ -593,9 +596,11 @@ struct AppendRow {
     }
   }
 
-  template <bool kMma>
-  __device__ __forceinline__ void patch(const AttnArgs& a, uint8_t* kt, int kvh, bool owner, int lane) const {
-    constexpr int kTile = kBlockTokens * D * (int)sizeof(T);
+  // `row` is the token's row within the tile (its block row, or that minus
+  // the half-block offset for 8-row tiles); kTile is the tile's bytes.
+  template <bool kMma, int kTile>
+  __device__ __forceinline__ void patch(const AttnArgs& a, uint8_t* kt, int row, int kvh, bool owner,
+                                        int lane) const {
     if (a.slot_mapping != nullptr) {
       if (slot < 0) return;
       if ((int64_t)slot != (int64_t)phys * kBlockTokens + tok) {
@@ -610,8 +615,8 @@ struct AppendRow {
       if (i < 2 * kRowChunks) {
         const int kv = i >= kRowChunks ? 1 : 0;
         const int c = i - kv * kRowChunks;
-        const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + tok * 128 + (((c & 7) ^ (tok & 7)) << 4)
-                             : tok * D * (int)sizeof(T) + c * 16;
+        const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4)
+                             : row * D * (int)sizeof(T) + c * 16;
         *reinterpret_cast<uint4*>(kt + kv * kTile + off) = v[j];
         if (owner)
           *reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? a.v_cache_w : a.k_cache_w) + dst + c * kVec) = v[j];
@@ -627,7 +632,10 @@ struct AppendRow {
 // ---------------------------------------------------------------------------
 template <typename T, int D, int HG>
 struct AttnConfig {
-  static constexpr int kTileBytes = kBlockTokens * D * (int)sizeof(T);  // one K or V tile
+  // Tile rows: a 16-token block, or half of one for fp32 at D >= 128 (8 KB
+  // blocks would leave room for one CTA per SM).
+  static constexpr int kRows = (sizeof(T) == 4 && D >= 128) ? 8 : kBlockTokens;
+  static constexpr int kTileBytes = kRows * D * (int)sizeof(T);  // one K or V tile
   static constexpr int kWarps = 4;
   // 1-byte (fp8) tiles: half the ring, so twice the CTAs fit on an SM.
   static constexpr int kStageBudget = sizeof(T) == 1 ? 48 * 1024 : 96 * 1024;
@@ -639,7 +647,7 @@ struct AttnConfig {
   static constexpr int kBarOffset = kTileArea;
   static constexpr int kFlagOffset = kBarOffset + kWarps * kStages * 8;
   static constexpr int kPbufOffset = kFlagOffset + ((kWarps * kStages * 4 + 15) / 16) * 16;
-  static constexpr int kSmemBytes = kPbufOffset + kWarps * HG * kBlockTokens * 4;
+  static constexpr int kSmemBytes = kPbufOffset + kWarps * HG * kRows * 4;
   static constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1 KB
   // fp8 at D=128: four CTAs (16 warps) per SM, the registers capped to fit.
   static constexpr int kMinCtas = (sizeof(T) == 1 && D == 128) ? 4 : 1;
@@ -652,8 +660,11 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   // T: query / output type; TC: cache type (T, or fp8 e4m3 with T 16-bit).
   using Cfg = AttnConfig<TC, D, HG>;
   constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+  constexpr int R = Cfg::kRows;             // tokens per tile
+  constexpr int kSubs = kBlockTokens / R;   // tiles per block
+  static_assert(!kMma || R == kBlockTokens, "tensor-core tiles are whole blocks");
   using Consumer = std::conditional_t<kMma, std::conditional_t<kFp8, MmaConsumerFp8<T, D>, MmaConsumer<T, D>>,
-                                      FmaConsumer<T, TC, D, HG>>;
+                                      FmaConsumer<T, TC, D, HG, R>>;
   static_assert(!kMma || HG == 8, "the tensor-core consumer covers 8 query heads");
   static_assert(!kAppend || std::is_same<T, TC>::value, "the fused append writes caches of the query type");
   constexpr int NW = Cfg::kWarps;
@@ -667,6 +678,14 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   const int head0 = kvh * a.group + chunk * HG;
   const int nheads = min(HG, a.group - chunk * HG);
 
+  // This warp's first 32 block ids do not depend on the context length: load
+  // them now, so the first copies wait on one memory round trip, not two.
+  const int32_t* table_row = a.block_tables + (size_t)seq * a.max_blocks_per_seq;
+  int ids_pre = 0;
+  {
+    const int b = part * a.part_blocks + ((threadIdx.x >> 5) + (threadIdx.x & 31) * Cfg::kWarps) / kSubs;
+    if (b < a.max_blocks_per_seq) ids_pre = table_row[b];
+  }
   int ctx = a.context_lens[seq];
   const int ctx_cap = a.max_blocks_per_seq * kBlockTokens;
   if (ctx < 0 || ctx > ctx_cap) {
@@ -679,7 +698,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   if (part == 0 && nparts > (int)gridDim.x && threadIdx.x == 0 && blockIdx.y == 0)
     attn_error(CF_DEVERR_CONTEXT_LEN);  // context_lens exceeds max_context_len
   const bool single = (nparts == 1);
-  const int last_blk = (kAppend && ctx > 0) ? (ctx - 1) / kBlockTokens : -1;
+  const int last_tok = (kAppend && ctx > 0) ? ctx - 1 : -1;
   const int pb0 = part * a.part_blocks;
   const int pb1 = min(nblk, pb0 + a.part_blocks);
 
@@ -691,7 +710,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   uint8_t* tiles = smem + (size_t)warp * S * 2 * TILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset) + warp * S;
   int* flags = reinterpret_cast<int*>(smem + Cfg::kFlagOffset) + warp * S;
-  float* pbuf = reinterpret_cast<float*>(smem + Cfg::kPbufOffset) + warp * HG * kBlockTokens;
+  float* pbuf = reinterpret_cast<float*>(smem + Cfg::kPbufOffset) + warp * HG * R;
 
   if (lane == 0) {
 #pragma unroll
@@ -704,16 +723,22 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   const T* qrow = reinterpret_cast<const T*>(a.q) + ((size_t)seq * a.num_heads + head0) * D;
   cons.init(qrow, nheads, a.scale_log2, lane);
 
-  // This warp's blocks: pb0 + warp + j*NW, j in [0, nb).
-  const int span = pb1 - pb0;
+  // The partition's tiles (R tokens each, kSubs per block) are dealt to the
+  // warps round-robin: this warp's tiles are u = warp + j*NW, j in [0, nb);
+  // tile u covers block pb0 + u / kSubs, rows (u % kSubs) * R ...
+  const int span = (pb1 - pb0) * kSubs;
   const int nb = span > warp ? (span - warp + NW - 1) / NW : 0;
-  const int32_t* table = a.block_tables + (size_t)seq * a.max_blocks_per_seq + pb0 + warp;
+  const int32_t* table = a.block_tables + (size_t)seq * a.max_blocks_per_seq + pb0;
   AppendRow<T, D> app;
   bool app_mine = false;
+  int app_u = -1;
   if constexpr (kAppend) {
-    if (last_blk >= pb0 && last_blk < pb1 && (last_blk - pb0) % NW == warp) {
-      app.load(a, seq, kvh, last_blk, ctx, lane);
-      app_mine = true;
+    if (last_tok >= pb0 * kBlockTokens && last_tok < pb1 * kBlockTokens) {
+      app_u = last_tok / R - pb0 * kSubs;
+      if (app_u % NW == warp) {
+        app.load(a, seq, kvh, last_tok / kBlockTokens, ctx, lane);
+        app_mine = true;
+      }
     }
   }
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k_cache);
@@ -721,11 +746,19 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
 
   auto fetch_ids = [&](int jbase) -> int {
     const int j = jbase + lane;
-    return j < nb ? table[(size_t)j * NW] : 0;
+    return j < nb ? table[(warp + j * NW) / kSubs] : 0;
   };
   auto issue = [&](int j, int phys) {  // lane 0 only
     const int s = j % S;
     const uint32_t bar = smem_addr(&bars[s]);
+    const int u = warp + j * NW;
+    const int sub = u % kSubs;
+    // a half-block tile past the context holds no tokens: nothing to load
+    if (kSubs > 1 && (pb0 + u / kSubs) * kBlockTokens + sub * R >= ctx) {
+      flags[s] = 0;
+      mbar_arrive(bar);
+      return;
+    }
     if (phys < 0 || (int64_t)phys >= a.num_blocks) {
       attn_error(CF_DEVERR_BLOCK_ID);
       flags[s] = 0;
@@ -747,13 +780,14 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
         tma_load_2d(smem_addr(kt + TILE + b * kBlockTokens * 128), &tmv, b * kBoxElems, row, bar);
       }
     } else {
-      const size_t off = ((size_t)phys * a.num_kv_heads + kvh) * (size_t)TILE;
+      const size_t off = (((size_t)phys * a.num_kv_heads + kvh) * kBlockTokens + (size_t)sub * R) * D *
+                         sizeof(TC);
       bulk_load(smem_addr(kt), kbase + off, TILE, bar);
       bulk_load(smem_addr(kt + TILE), vbase + off, TILE, bar);
     }
   };
 
-  int ids = fetch_ids(0);
+  int ids = ids_pre;  // = fetch_ids(0) for every unit the warp uses
   const int pro = nb < S ? nb : S;
   for (int j = 0; j < pro; ++j) {
     const int phys = __shfl_sync(0xffffffffu, ids, j);
@@ -778,12 +812,13 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
       ok = false;
       break;
     }
-    const int blk = pb0 + warp + i * NW;
-    const int ntok = min(kBlockTokens, ctx - blk * kBlockTokens);
+    const int u = warp + i * NW;
+    const int tok0 = (pb0 + u / kSubs) * kBlockTokens + (u % kSubs) * R;  // first token of the tile
+    const int ntok = min(R, ctx - tok0);
     if (flags[s]) {
       uint8_t* kt = tiles + (size_t)s * 2 * TILE;
       if constexpr (kAppend) {
-        if (app_mine && blk == last_blk) app.template patch<kMma>(a, kt, kvh, chunk == 0, lane);
+        if (app_mine && u == app_u) app.template patch<kMma, TILE>(a, kt, last_tok - tok0, kvh, chunk == 0, lane);
       }
       cons.block(kt, kt + TILE, ntok, pbuf, lane);
     }
