@@ -678,11 +678,13 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   const int head0 = kvh * a.group + chunk * HG;
   const int nheads = min(HG, a.group - chunk * HG);
 
-  // This warp's first 32 block ids do not depend on the context length: load
-  // them now, so the first copies wait on one memory round trip, not two.
-  const int32_t* table_row = a.block_tables + (size_t)seq * a.max_blocks_per_seq;
+  // FMA consumers: this warp's first 32 block ids do not depend on the
+  // context length, so load them now and the first copies wait on one memory
+  // round trip, not two.  (The register-capped tensor-core consumers load
+  // them after their set-up.)
   int ids_pre = 0;
-  {
+  if constexpr (!kMma) {
+    const int32_t* table_row = a.block_tables + (size_t)seq * a.max_blocks_per_seq;
     const int b = part * a.part_blocks + ((threadIdx.x >> 5) + (threadIdx.x & 31) * Cfg::kWarps) / kSubs;
     if (b < a.max_blocks_per_seq) ids_pre = table_row[b];
   }
@@ -787,7 +789,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     }
   };
 
-  int ids = ids_pre;  // = fetch_ids(0) for every unit the warp uses
+  int ids = kMma ? fetch_ids(0) : ids_pre;  // ids_pre = fetch_ids(0) for every tile the warp uses
   const int pro = nb < S ? nb : S;
   for (int j = 0; j < pro; ++j) {
     const int phys = __shfl_sync(0xffffffffu, ids, j);
