@@ -132,6 +132,11 @@ SIGNATURES = {
     ),
     "cf_swap_blocks": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_void_p]),
     "cf_swap_blocks_dma": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_void_p]),
+    "cf_execute_block_ops": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int32, c_void_p, c_int32,
+         c_void_p, c_int32, c_void_p],
+    ),
     "cf_compact_kv_cache": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int64,

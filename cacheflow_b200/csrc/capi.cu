@@ -405,6 +405,51 @@ cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
   return CF_OK;
 }
 
+cf_status cf_execute_block_ops(void* gpu_key_cache, void* gpu_value_cache, void* cpu_key_cache,
+                               void* cpu_value_cache, int64_t block_size_bytes,
+                               int64_t num_gpu_blocks, int64_t num_cpu_blocks,
+                               const int64_t* swaps_out, int32_t num_swaps_out,
+                               const int64_t* swaps_in, int32_t num_swaps_in,
+                               const int64_t* copies, int32_t num_copies, void* stream) {
+  if (block_size_bytes <= 0 || num_gpu_blocks < 0 || num_cpu_blocks < 0 || num_swaps_out < 0 ||
+      num_swaps_in < 0 || num_copies < 0)
+    return CF_ERR_INVALID_ARGUMENT;
+  // Every id is checked on the host before anything is enqueued.
+  auto ok = [](const int64_t* pairs, int32_t n, int64_t src_lim, int64_t dst_lim) {
+    if (n > 0 && pairs == nullptr) return false;
+    for (int32_t i = 0; i < n; ++i)
+      if (pairs[2 * i] < 0 || pairs[2 * i] >= src_lim || pairs[2 * i + 1] < 0 || pairs[2 * i + 1] >= dst_lim)
+        return false;
+    return true;
+  };
+  if (!ok(swaps_out, num_swaps_out, num_gpu_blocks, num_cpu_blocks) ||
+      !ok(swaps_in, num_swaps_in, num_cpu_blocks, num_gpu_blocks) ||
+      !ok(copies, num_copies, num_gpu_blocks, num_gpu_blocks))
+    return CF_ERR_INVALID_ARGUMENT;
+  if ((num_swaps_out + num_swaps_in + num_copies) > 0 && (!gpu_key_cache || !gpu_value_cache))
+    return CF_ERR_INVALID_ARGUMENT;
+  if ((num_swaps_out + num_swaps_in) > 0 && (!cpu_key_cache || !cpu_value_cache))
+    return CF_ERR_INVALID_ARGUMENT;
+  // Swap-outs free GPU blocks that swap-ins and copies may then reuse.
+  const struct {
+    void* src;
+    void* dst;
+    const int64_t* pairs;
+    int32_t n;
+  } steps[6] = {{gpu_key_cache, cpu_key_cache, swaps_out, num_swaps_out},
+                {gpu_value_cache, cpu_value_cache, swaps_out, num_swaps_out},
+                {cpu_key_cache, gpu_key_cache, swaps_in, num_swaps_in},
+                {cpu_value_cache, gpu_value_cache, swaps_in, num_swaps_in},
+                {gpu_key_cache, gpu_key_cache, copies, num_copies},
+                {gpu_value_cache, gpu_value_cache, copies, num_copies}};
+  for (const auto& st : steps) {
+    if (st.n == 0) continue;
+    const cf_status r = cf_swap_blocks_dma(st.src, st.dst, st.pairs, st.n, block_size_bytes, stream);
+    if (r != CF_OK) return r;
+  }
+  return CF_OK;
+}
+
 cf_status cf_compact_kv_cache(void* key_cache, void* value_cache, const int32_t* src_block_ids,
                               const int32_t* dst_block_ids, int32_t num_moves,
                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,

@@ -42,6 +42,7 @@ __all__ = [
     "swap_blocks_dma",
     "compact_kv_cache",
     "memset_blocks",
+    "execute_block_ops",
     "compaction_plan",
     "check_compaction_plan",
     "device_errors",
@@ -421,6 +422,34 @@ def memset_blocks(cache, block_ids) -> None:
     check(lib.cf_memset_blocks(_ptr(cache), _ptr(block_ids), block_ids.shape[0], _block_bytes(cache),
                                cache.shape[0], _stream(cache)),
           "cf_memset_blocks")
+
+
+def execute_block_ops(gpu_key_cache, gpu_value_cache, cpu_key_cache, cpu_value_cache, swaps_out=None,
+                      swaps_in=None, copies=None) -> None:
+    """One scheduling step's block operations (SchedulerOutput::block_swaps_out,
+    block_swaps_in, block_copies): swap-outs, swap-ins, then copy-on-write
+    copies, for K and V, on the copy engines.  Pair lists are host int64
+    arrays [n, 2] of (src, dst) block ids."""
+    lib = _lib.load()
+
+    def host_pairs(x):
+        if x is None:
+            return None, 0
+        a = np.ascontiguousarray(np.asarray(x, dtype=np.int64).reshape(-1, 2))
+        return a, a.shape[0]
+
+    so, nso = host_pairs(swaps_out)
+    si, nsi = host_pairs(swaps_in)
+    cp, ncp = host_pairs(copies)
+    cpu_k = _ptr(cpu_key_cache) if cpu_key_cache is not None else None
+    cpu_v = _ptr(cpu_value_cache) if cpu_value_cache is not None else None
+    ncpu = cpu_key_cache.shape[0] if cpu_key_cache is not None else 0
+    check(lib.cf_execute_block_ops(_ptr(gpu_key_cache), _ptr(gpu_value_cache), cpu_k, cpu_v,
+                                   _block_bytes(gpu_key_cache), gpu_key_cache.shape[0], ncpu,
+                                   None if so is None else so.ctypes.data, nso,
+                                   None if si is None else si.ctypes.data, nsi,
+                                   None if cp is None else cp.ctypes.data, ncp, _stream(gpu_key_cache)),
+          "cf_execute_block_ops")
 
 
 def compaction_plan(used: np.ndarray) -> tuple[np.ndarray, np.ndarray]:

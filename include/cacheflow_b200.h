@@ -294,6 +294,24 @@ CF_API cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
                              int32_t num_pairs, int64_t block_size_bytes,
                              void* stream);
 
+/* Executes one scheduling step's block operations -- CacheFlow's
+ * SchedulerOutput::block_swaps_out, block_swaps_in and block_copies
+ * (scheduler.h:22-29, produced at scheduler.cpp:223,252) -- on `stream`, in
+ * that order and for both K and V: swap-outs (GPU block -> CPU block),
+ * swap-ins (CPU block -> GPU block), then copy-on-write copies (GPU -> GPU).
+ * Each list is HOST int64 [n, 2] of (src, dst) block ids; every id is checked
+ * against its pool before anything is enqueued (CF_ERR_INVALID_ARGUMENT).
+ * Runs of consecutive ids become single cudaMemcpyAsync calls on the copy
+ * engines, so no SM time is used; within one list the pairs apply in order.
+ * CPU pools should be pinned for the copies to be asynchronous. */
+CF_API cf_status cf_execute_block_ops(void* gpu_key_cache, void* gpu_value_cache,
+                                      void* cpu_key_cache, void* cpu_value_cache,
+                                      int64_t block_size_bytes, int64_t num_gpu_blocks,
+                                      int64_t num_cpu_blocks, const int64_t* swaps_out,
+                                      int32_t num_swaps_out, const int64_t* swaps_in,
+                                      int32_t num_swaps_in, const int64_t* copies,
+                                      int32_t num_copies, void* stream);
+
 /* In-place defragmentation: for each i, K and V block dst_ids[i] := block
  * src_ids[i] (src == dst is skipped).  All moves run concurrently, so the
  * plan must not overlap: no destination may also be a source, and no

@@ -128,6 +128,11 @@ def test_invalid_arguments_rejected_without_gpu(cflib):
     p.num_blocks = 64
     assert cflib.cf_paged_attention_append_v2(ctypes.byref(p), 1 << 20, 1 << 20, None, es, es, es, 1, None) == \
         _lib.CF_ERR_WORKSPACE
+    # scheduler block ops: ids are range-checked on the host before anything runs
+    pairs = (ctypes.c_int64 * 2)(0, 5)
+    assert cflib.cf_execute_block_ops(None, None, None, None, 4096, 4, 4, None, 0, None, 0, None, 0, None) == _lib.CF_OK
+    assert cflib.cf_execute_block_ops(1 << 20, 1 << 20, 1 << 21, 1 << 21, 4096, 8, 4, pairs, 1, None, 0, None, 0,
+                                      None) == _lib.CF_ERR_INVALID_ARGUMENT  # cpu id 5 >= 4
     # decode-input builder
     assert cflib.cf_build_decode_inputs(None, None, None, 0, 4, 16, None, None, None, None) == _lib.CF_OK
     assert cflib.cf_build_decode_inputs(None, None, None, 3, 4, 16, None, None, None, None) == \

@@ -242,3 +242,39 @@ def test_reference_v1_short_contexts_agree(cflib, oracle_mod):
         want = oracle_mod.paged_attention(q, k, v, tables, np.array(ctx, np.int32), scale)
         assert_close(as_f64(theirs), want, "f32", "reference V1 vs oracle")
         assert_close(as_f64(ours), want, "f32", "ours vs oracle")
+
+
+def test_execute_block_ops_matches_sequential_application(cflib):
+    """One step's scheduler block ops (swap-outs, swap-ins, then COW copies,
+    for K and V) equal applying the lists in that order on the host."""
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(31)
+    ngpu, ncpu, shape = 24, 16, (8, 16, 64)
+    gk = torch.from_numpy(rng.standard_normal((ngpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    gv = torch.from_numpy(rng.standard_normal((ngpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    ck = torch.from_numpy(rng.standard_normal((ncpu,) + shape).astype(np.float32)).to(torch.bfloat16).pin_memory()
+    cv = torch.from_numpy(rng.standard_normal((ncpu,) + shape).astype(np.float32)).to(torch.bfloat16).pin_memory()
+    # swap-outs include a run of consecutive ids (one merged copy)
+    swaps_out = np.array([[3, 0], [4, 1], [5, 2], [10, 7]], np.int64)
+    swaps_in = np.array([[9, 3], [12, 20]], np.int64)       # GPU block 3 reused after its swap-out
+    copies = np.array([[20, 21], [0, 5], [7, 8]], np.int64)  # copies see the swapped-in block 20
+    want = [t.clone() for t in (gk, gv, ck, cv)]
+    for src, dst in swaps_out:
+        want[2][dst] = want[0][src]
+        want[3][dst] = want[1][src]
+    for src, dst in swaps_in:
+        want[0][dst] = want[2][src]
+        want[1][dst] = want[3][src]
+    for src, dst in copies:
+        want[0][dst] = want[0][src]
+        want[1][dst] = want[1][src]
+    dk, dv = gk.cuda(), gv.cuda()
+    ops.execute_block_ops(dk, dv, ck, cv, swaps_out, swaps_in, copies)
+    torch.cuda.synchronize()
+    assert torch.equal(dk.cpu(), want[0]) and torch.equal(dv.cpu(), want[1])
+    assert torch.equal(ck, want[2]) and torch.equal(cv, want[3])
+    with pytest.raises(ops.CacheFlowError):  # a CPU id past the pool: nothing is enqueued
+        ops.execute_block_ops(dk, dv, ck, cv, swaps_out=np.array([[0, ncpu]], np.int64))
