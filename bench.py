@@ -274,7 +274,7 @@ def run_ours(args):
     nc = len(w.chunk_context_lens) if chunked else 0
     # decode-only batches (one new token per row, at its newest position)
     # append it inside the attention launch unless --append separate
-    fused = args.append == "fused" and not w.has_chunks and T == S and not fp8
+    fused = args.append == "fused" and not w.has_chunks and T == S
     new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
                           max_chunks=nc, fused_append=fused, kv_scales=(kv_scale, kv_scale) if fp8 else None,
@@ -310,9 +310,11 @@ def run_ours(args):
     def step(record=False):
         if pairs is not None:
             ops.copy_blocks(k_cache, v_cache, pairs)
-        if fp8:
+        if fused:
+            pass
+        elif fp8:
             ops.reshape_and_cache_fp8(k_new, v_new, k_cache, v_cache, slots, kv_scale, kv_scale)
-        elif not fused:
+        else:
             ops.reshape_and_cache(k_new, v_new, k_cache, v_cache, slots)
         if record:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -427,7 +429,7 @@ def run_ours(args):
         peak, peak_kind = hbm_peak()
         alg_bytes = kv_step + w.qo_bytes() + w.table_bytes()
         if fused:  # the appended rows: new K/V read, cache rows written, slots read
-            alg_bytes += 2 * 2 * T * Hkv * D * k_cache.element_size() + 4 * T
+            alg_bytes += 2 * T * Hkv * D * (k_new.element_size() + k_cache.element_size()) + 4 * T
         achieved = alg_bytes / (att_ms * 1e-3) / 1e9
         value = kv_total / (ms_step * 1e-3) / 1e9
         line = {

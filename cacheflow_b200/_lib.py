@@ -109,6 +109,16 @@ SIGNATURES = {
         c_int32,
         [POINTER(AttentionParams), c_float, c_float, c_void_p, c_void_p, c_void_p, c_int32, c_void_p],
     ),
+    "cf_paged_attention_fp8_append_v1": (
+        c_int32,
+        [POINTER(AttentionParams), c_float, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+         c_void_p],
+    ),
+    "cf_paged_attention_fp8_append_v2": (
+        c_int32,
+        [POINTER(AttentionParams), c_float, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_int32, c_void_p],
+    ),
     "cf_reshape_and_cache_fp8": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int64,

@@ -274,6 +274,37 @@ cf_status cf_paged_attention_fp8_v2(const cf_paged_attention_params* p, float k_
                 fp8_extras(k_scale, v_scale));
 }
 
+cf_status cf_paged_attention_fp8_append_v1(const cf_paged_attention_params* p, float k_scale,
+                                           float v_scale, const void* key, const void* value,
+                                           const int32_t* slot_mapping, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+  const cf_status st = check_fp8(p, k_scale, v_scale);
+  if (st != CF_OK) return st;
+  if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
+  Extras x = fp8_extras(k_scale, v_scale);
+  x.key = key;
+  x.value = value;
+  x.slots = slot_mapping;
+  return run_v1(p, workspace, workspace_bytes, stream, x);
+}
+
+cf_status cf_paged_attention_fp8_append_v2(const cf_paged_attention_params* p, float k_scale,
+                                           float v_scale, const void* key, const void* value,
+                                           const int32_t* slot_mapping, float* exp_sums,
+                                           float* max_logits, float* tmp_output,
+                                           int32_t num_partitions, void* stream) {
+  const cf_status st = check_fp8(p, k_scale, v_scale);
+  if (st != CF_OK) return st;
+  if (!key || !value || !aligned16(key) || !aligned16(value)) return CF_ERR_INVALID_ARGUMENT;
+  if (p->num_seqs > 0 && p->num_blocks <= 0) return CF_ERR_INVALID_ARGUMENT;
+  Extras x = fp8_extras(k_scale, v_scale);
+  x.key = key;
+  x.value = value;
+  x.slots = slot_mapping;
+  return run_v2(p, exp_sums, max_logits, tmp_output, num_partitions, stream, x);
+}
+
 cf_status cf_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
                                    void* value_cache, const int32_t* slot_mapping,
                                    int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,

@@ -222,6 +222,18 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Per-thread asynchronous copies global -> shared (16 bytes: both addresses
+// 16-byte aligned; 4 bytes: 4-byte aligned), waited for by the issuing thread
+// with cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // 2-D tiled TMA load (tensor map), completion counted on `bar`.
 // x is the innermost coordinate (elements); callers keep x * sizeof(T) a
 // multiple of 16 bytes.

@@ -84,6 +84,7 @@ struct AttnArgs {
   void* k_cache_w;              // the caches, written by the append
   void* v_cache_w;
   float v_scale;                // fp8 caches: V = stored * v_scale (else 1)
+  float k_scale;                // fp8 caches: K = stored * k_scale (appends store K / k_scale)
 };
 
 // ---------------------------------------------------------------------------
@@ -555,34 +556,38 @@ struct MmaConsumerFp8 {
 
 // ---------------------------------------------------------------------------
 // Fused append: the warp that will hold block `blk` (the one with the row's
-// newest token) loads the new K/V row, the block id and the slot before its
-// pipeline starts (so the patch waits on nothing); when that block's tile
-// lands it overwrites the token's row in the tile -- in the tile's own layout:
-// row-major for the FMA consumer, 64-element boxes with the 128-byte swizzle
-// for the MMA consumer -- and, in the CTA of head chunk 0 (`owner`), stores it
-// into the cache, which is what reshape_and_cache (kv_cache_kernels.cu:34-40)
-// does with slot = block_tables[s][blk] * 16 + (ctx - 1) % 16.  A slot_mapping
+// newest token) copies the new K/V row, the block id and the slot into shared
+// memory (cp.async) before its pipeline starts, so the patch waits on nothing
+// and no registers are held across the loop; when that block's tile lands it
+// overwrites the token's row in the tile -- in the tile's own layout:
+// row-major for the FMA consumer, 128-byte boxes with the 128-byte swizzle
+// for the MMA consumers (e4m3 bytes for fp8 caches) -- and, in the CTA of
+// head chunk 0 (`owner`), stores it into the cache, which is what
+// reshape_and_cache (kv_cache_kernels.cu:34-40) does with
+// slot = block_tables[s][blk] * 16 + (ctx - 1) % 16.  A slot_mapping
 // entry that is negative appends nothing; one that is not that slot is
 // recorded (CF_DEVERR_SLOT) and appends nothing.  Other CTAs of the same row
 // may read the cache row while it is written; they overwrite it in their own
 // tile.
 // ---------------------------------------------------------------------------
-template <typename T, int D>
+template <typename T, typename TC, int D>
 struct AppendRow {
-  static constexpr int kRowChunks = D * (int)sizeof(T) / 16;  // 16-byte chunks of one row
-  static constexpr int kPerLane = (2 * kRowChunks + 31) / 32;  // K then V
+  static constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+  static constexpr int kRowBytes = D * (int)sizeof(T);         // one new K or V row
+  static constexpr int kRowChunks = kRowBytes / 16;              // its 16-byte chunks
+  static constexpr int kPerLane = (2 * kRowChunks + 31) / 32;    // K then V
   static constexpr int kVec = 16 / (int)sizeof(T);
-  uint4 v[kPerLane];
-  int32_t phys;
-  int32_t slot;  // slot_mapping[seq] (unused without a slot_mapping)
-  int tok;
+  static constexpr int kOut = kVec * (int)sizeof(TC);  // cache bytes of one chunk (8 for fp8)
+  // Staging area in shared memory: the K row, the V row, then four int32:
+  // the block id, the slot_mapping entry, the token's position and whether
+  // this CTA stores the row to the cache.
+  static constexpr int kStageBytes = 2 * kRowBytes + 16;
 
-  // Issues the loads only: nothing here waits for them, so the warp's copy
-  // pipeline starts at once and the values arrive while it streams.
-  __device__ __forceinline__ void load(const AttnArgs& a, int seq, int kvh, int blk, int ctx, int lane) {
-    tok = ctx - 1 - blk * kBlockTokens;
-    phys = a.block_tables[(size_t)seq * a.max_blocks_per_seq + blk];
-    slot = a.slot_mapping != nullptr ? a.slot_mapping[seq] : 0;
+  // Issues asynchronous copies only (nothing is held in registers and nothing
+  // here waits for them), so the warp's copy pipeline starts at once and the
+  // row arrives while it streams.
+  __device__ __forceinline__ static void load(const AttnArgs& a, uint8_t* stage, int seq, int kvh, int pos,
+                                              bool owner, int lane) {
     const size_t src = ((size_t)seq * a.num_kv_heads + kvh) * D;
 #pragma unroll
     for (int j = 0; j < kPerLane; ++j) {
@@ -590,36 +595,95 @@ struct AppendRow {
       if (i < 2 * kRowChunks) {
         const int kv = i >= kRowChunks ? 1 : 0;
         const int c = i - kv * kRowChunks;
-        v[j] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(kv ? a.new_v : a.new_k) + src +
-                                               c * kVec);
+        cp_async16(smem_addr(stage + i * 16), reinterpret_cast<const T*>(kv ? a.new_v : a.new_k) + src + c * kVec);
       }
+    }
+    if (lane == 0) {
+      int32_t* w = reinterpret_cast<int32_t*>(stage + 2 * kRowBytes);
+      cp_async4(smem_addr(w), a.block_tables + (size_t)seq * a.max_blocks_per_seq + pos / kBlockTokens);
+      if (a.slot_mapping != nullptr) cp_async4(smem_addr(w + 1), a.slot_mapping + seq);
+      w[2] = pos;
+      w[3] = owner ? 1 : 0;
+    }
+    cp_async_commit();
+  }
+
+  // Called when the tile holding the token (R rows) has landed.  kTile is the
+  // tile's bytes.  An fp8 cache takes each element as e4m3(x / scale),
+  // rounded to nearest even and saturated to +-448, exactly as
+  // reshape_and_cache_fp8 stores it.
+  template <bool kMma, int kTile, int R>
+  __device__ __forceinline__ static void patch(const AttnArgs& a, const uint8_t* stage, uint8_t* kt, int kvh,
+                                               int lane) {
+    if constexpr (kFp8) {
+      patch_call<kMma, kTile, R>(a.k_cache_w, a.v_cache_w, a.slot_mapping != nullptr, a.num_kv_heads, a.k_scale,
+                                 a.v_scale, stage, kt, kvh, lane);
+    } else {
+      patch_body<kMma, kTile, R>(a.k_cache_w, a.v_cache_w, a.slot_mapping != nullptr, a.num_kv_heads, a.k_scale,
+                                 a.v_scale, stage, kt, kvh, lane);
     }
   }
 
-  // `row` is the token's row within the tile (its block row, or that minus
-  // the half-block offset for 8-row tiles); kTile is the tile's bytes.
-  template <bool kMma, int kTile>
-  __device__ __forceinline__ void patch(const AttnArgs& a, uint8_t* kt, int row, int kvh, bool owner,
-                                        int lane) const {
-    if (a.slot_mapping != nullptr) {
+  // The fp8 kernels run register-capped (four CTAs per SM): an out-of-line
+  // call keeps the conversion's registers out of the streaming loop.
+  template <bool kMma, int kTile, int R>
+  __device__ __noinline__ static void patch_call(void* kc, void* vc, bool has_slots, int32_t num_kv_heads,
+                                                 float k_scale, float v_scale, const uint8_t* stage, uint8_t* kt,
+                                                 int kvh, int lane) {
+    patch_body<kMma, kTile, R>(kc, vc, has_slots, num_kv_heads, k_scale, v_scale, stage, kt, kvh, lane);
+  }
+
+  template <bool kMma, int kTile, int R>
+  __device__ __forceinline__ static void patch_body(void* kc, void* vc, bool has_slots, int32_t num_kv_heads,
+                                                    float k_scale, float v_scale, const uint8_t* stage,
+                                                    uint8_t* kt, int kvh, int lane) {
+    cp_async_wait_all();
+    __syncwarp();  // lane 0's block id and slot are visible to the warp
+    const int32_t* w = reinterpret_cast<const int32_t*>(stage + 2 * kRowBytes);
+    const int32_t phys = w[0];
+    const int pos = w[2];
+    const bool owner = w[3] != 0;
+    const int row = pos % R;              // the token's row within the tile
+    const int tok = pos % kBlockTokens;   // and within its block
+    if (has_slots) {
+      const int32_t slot = w[1];
       if (slot < 0) return;
       if ((int64_t)slot != (int64_t)phys * kBlockTokens + tok) {
         if (owner && lane == 0) attn_error(CF_DEVERR_SLOT);
         return;
       }
     }
-    const size_t dst = (((size_t)phys * a.num_kv_heads + kvh) * kBlockTokens + tok) * D;
+    const size_t dst = (((size_t)phys * num_kv_heads + kvh) * kBlockTokens + tok) * D * sizeof(TC);
 #pragma unroll
     for (int j = 0; j < kPerLane; ++j) {
       const int i = lane + 32 * j;
       if (i < 2 * kRowChunks) {
         const int kv = i >= kRowChunks ? 1 : 0;
         const int c = i - kv * kRowChunks;
-        const int off = kMma ? (c >> 3) * (kBlockTokens * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4)
-                             : row * D * (int)sizeof(T) + c * 16;
-        *reinterpret_cast<uint4*>(kt + kv * kTile + off) = v[j];
-        if (owner)
-          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? a.v_cache_w : a.k_cache_w) + dst + c * kVec) = v[j];
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 16);
+        const int p = c * kOut;  // byte of the chunk within the cache row
+        const int off = kMma ? (p >> 7) * (kBlockTokens * 128) + row * 128 +
+                                   ((((p >> 4) & 7) ^ (row & 7)) << 4) + (p & 15)
+                             : row * D * (int)sizeof(TC) + p;
+        uint8_t* cache = reinterpret_cast<uint8_t*>(kv ? vc : kc) + dst + p;
+        if constexpr (kFp8) {
+          const float sc = kv ? v_scale : k_scale;
+          const uint32_t x[4] = {v.x, v.y, v.z, v.w};
+          uint32_t q[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float f[4];
+            unpack_word<T>(x[2 * h], f);
+            unpack_word<T>(x[2 * h + 1], f + 2);
+            q[h] = (uint32_t)f2_to_e4m3x2(__fdiv_rn(f[0], sc), __fdiv_rn(f[1], sc)) |
+                   ((uint32_t)f2_to_e4m3x2(__fdiv_rn(f[2], sc), __fdiv_rn(f[3], sc)) << 16);
+          }
+          *reinterpret_cast<uint2*>(kt + kv * kTile + off) = make_uint2(q[0], q[1]);
+          if (owner) *reinterpret_cast<uint2*>(cache) = make_uint2(q[0], q[1]);
+        } else {
+          *reinterpret_cast<uint4*>(kt + kv * kTile + off) = v;
+          if (owner) *reinterpret_cast<uint4*>(cache) = v;
+        }
       }
     }
     fence_proxy_async_smem();  // a later TMA write of this tile follows these stores
@@ -666,7 +730,8 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   using Consumer = std::conditional_t<kMma, std::conditional_t<kFp8, MmaConsumerFp8<T, D>, MmaConsumer<T, D>>,
                                       FmaConsumer<T, TC, D, HG, R>>;
   static_assert(!kMma || HG == 8, "the tensor-core consumer covers 8 query heads");
-  static_assert(!kAppend || std::is_same<T, TC>::value, "the fused append writes caches of the query type");
+  static_assert(!kAppend || std::is_same<T, TC>::value || (kFp8 && sizeof(T) == 2),
+                "the fused append writes caches of the query type, or fp8 ones");
   constexpr int NW = Cfg::kWarps;
   constexpr int S = Cfg::kStages;
   constexpr int TILE = Cfg::kTileBytes;
@@ -731,16 +796,13 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   const int span = (pb1 - pb0) * kSubs;
   const int nb = span > warp ? (span - warp + NW - 1) / NW : 0;
   const int32_t* table = a.block_tables + (size_t)seq * a.max_blocks_per_seq + pb0;
-  AppendRow<T, D> app;
-  bool app_mine = false;
-  int app_u = -1;
+  using App = AppendRow<T, TC, D>;
   if constexpr (kAppend) {
-    if (last_tok >= pb0 * kBlockTokens && last_tok < pb1 * kBlockTokens) {
-      app_u = last_tok / R - pb0 * kSubs;
-      if (app_u % NW == warp) {
-        app.load(a, seq, kvh, last_tok / kBlockTokens, ctx, lane);
-        app_mine = true;
-      }
+    // The warp whose tiles include the newest token's starts copying its row.
+    if (last_tok >= pb0 * kBlockTokens && last_tok < pb1 * kBlockTokens &&
+        (last_tok / R - pb0 * kSubs) % NW == warp) {
+      // staging: App::kStageBytes past the configuration's shared memory
+      App::load(a, smem + Cfg::kSmemBytes, seq, kvh, last_tok, chunk == 0, lane);
     }
   }
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k_cache);
@@ -796,8 +858,14 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     if (lane == 0) issue(j, phys);
   }
 
+  // The streaming loop.  With kAppend the newest token's tile is the last
+  // tile of the warp that holds it (the partition's highest tile, or the one
+  // before an empty half-block tile), so the loop stops one step short and
+  // that step runs peeled below, with the patch: the loop itself stays the
+  // plain one (the fp8 kernels have no registers to spare in it).
   bool ok = true;
-  for (int i = 0; i < nb; ++i) {
+  const int nmain = kAppend ? nb - 1 : nb;
+  for (int i = 0; i < nmain; ++i) {
     const int s = i % S;
     const uint32_t parity = (uint32_t)(i / S) & 1u;
     const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), parity);
@@ -819,9 +887,6 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     const int ntok = min(R, ctx - tok0);
     if (flags[s]) {
       uint8_t* kt = tiles + (size_t)s * 2 * TILE;
-      if constexpr (kAppend) {
-        if (app_mine && u == app_u) app.template patch<kMma, TILE>(a, kt, last_tok - tok0, kvh, chunk == 0, lane);
-      }
       cons.block(kt, kt + TILE, ntok, pbuf, lane);
     }
     __syncwarp();
@@ -830,6 +895,36 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
       if ((jn & 31) == 0) ids = fetch_ids(jn);
       const int phys = __shfl_sync(0xffffffffu, ids, jn & 31);
       if (lane == 0) issue(jn, phys);
+    }
+  }
+  if constexpr (kAppend) {
+    // The last step: no stage is refilled after it.
+    const int i = nb - 1;
+    if (ok && i >= 0) {
+      const int s = i % S;
+      const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u);
+      if (!__all_sync(0xffffffffu, ready)) {
+        if (lane == 0) {  // as in the loop: wait (bounded) once more for the copy in flight
+          attn_error(CF_DEVERR_TIMEOUT);
+          mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u);
+        }
+        ok = false;
+      } else {
+        const int u = warp + i * NW;
+        const int tok0 = (pb0 + u / kSubs) * kBlockTokens + (u % kSubs) * R;
+        if (flags[s]) {
+          uint8_t* kt = tiles + (size_t)s * 2 * TILE;
+          // whether this warp holds the newest token, recomputed here from
+          // the context length so nothing extra stays live across the loop
+          const int lt = ctx - 1;
+          const int p1 = min((ctx + kBlockTokens - 1) / kBlockTokens, pb0 + a.part_blocks);
+          if (ctx > 0 && lt >= pb0 * kBlockTokens && lt < p1 * kBlockTokens &&
+              (lt / R - pb0 * kSubs) % NW == warp)
+            App::template patch<kMma, TILE, R>(a, smem + Cfg::kSmemBytes, kt, kvh, lane);
+          cons.block(kt, kt + TILE, min(R, ctx - tok0), pbuf, lane);
+        }
+      }
+      __syncwarp();
     }
   }
 
@@ -1048,11 +1143,12 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
   using Cfg = AttnConfig<TC, D, HG>;
   const cf_paged_attention_params& p = *l.p;
   a.head_chunks = (a.group + HG - 1) / HG;
-  cf_status st = ensure_smem<T, TC, D, HG, kMma, kAppend>(Cfg::kSmemAlloc);
+  const int smem = Cfg::kSmemAlloc + (kAppend ? AppendRow<T, TC, D>::kStageBytes : 0);
+  cf_status st = ensure_smem<T, TC, D, HG, kMma, kAppend>(smem);
   if (st != CF_OK) return st;
   dim3 grid((unsigned)grid_x, (unsigned)(p.num_kv_heads * a.head_chunks), (unsigned)p.num_seqs);
   paged_attention_kernel<T, TC, D, HG, kMma, kAppend>
-      <<<grid, Cfg::kWarps * 32, Cfg::kSmemAlloc, l.stream>>>(a, maps.k, maps.v);
+      <<<grid, Cfg::kWarps * 32, smem, l.stream>>>(a, maps.k, maps.v);
   st = check_launch();
   if (st != CF_OK || l.part_max == nullptr || grid_x == 1) return st;
 
@@ -1140,8 +1236,8 @@ template <typename T>
 cf_status launch_type(const AttnLaunch& l, const AttnArgs& a, int grid_x) {
   if (l.cache_dtype == CF_FP8_E4M3) {
     if constexpr (sizeof(T) == 2) {
-      if (a.new_k != nullptr) return CF_ERR_UNSUPPORTED;
-      return launch_head_dim<T, __nv_fp8_e4m3, false>(l, a, grid_x);
+      return a.new_k != nullptr ? launch_head_dim<T, __nv_fp8_e4m3, true>(l, a, grid_x)
+                                : launch_head_dim<T, __nv_fp8_e4m3, false>(l, a, grid_x);
     }
     return CF_ERR_UNSUPPORTED;
   }
@@ -1179,6 +1275,7 @@ cf_status launch_paged_attention(const AttnLaunch& l) {
   a.part_out = l.part_out;
   a.scale_log2 = p.scale * kLog2e * l.k_scale;
   a.v_scale = l.v_scale;
+  a.k_scale = l.k_scale;
   a.num_heads = p.num_heads;
   a.num_kv_heads = p.num_kv_heads;
   a.group = p.num_heads / p.num_kv_heads;

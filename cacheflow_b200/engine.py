@@ -109,18 +109,29 @@ class DecodeEngine:
         S = num_seqs
         if self.fp8:
             ks, vs = self.kv_scales
-            if new is not None:
+            fused = new is not None and self.fused_append
+            if new is not None and not fused:
                 ops.reshape_and_cache_fp8(new[0], new[1], self.k, self.v, new[2], ks, vs)
+            extra = 1 if new is not None and not fused else 0
             if max_context_len <= V1_MAX_CONTEXT:
-                ops.paged_attention_fp8_v1(out, q, self.k, self.v, bt, cl, ks, vs, None, max_context_len,
-                                           workspace=self.workspace)
+                if fused:
+                    ops.paged_attention_fp8_append_v1(out, q, new[0], new[1], self.k, self.v, bt, cl, ks, vs, new[2],
+                                                      None, max_context_len, workspace=self.workspace)
+                else:
+                    ops.paged_attention_fp8_v1(out, q, self.k, self.v, bt, cl, ks, vs, None, max_context_len,
+                                               workspace=self.workspace)
                 split = self.workspace is not None and ops.paged_attention_v1_workspace_size(
                     q, self.k, bt, max_context_len) > 0
-                self.launches_per_step = (2 if split else 1) + (1 if new is not None else 0)
+                self.launches_per_step = (2 if split else 1) + extra
             else:
-                ops.paged_attention_fp8_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q,
-                                           self.k, self.v, bt, cl, ks, vs, None, max_context_len)
-                self.launches_per_step = 2 + (1 if new is not None else 0)
+                if fused:
+                    ops.paged_attention_fp8_append_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S],
+                                                      q, new[0], new[1], self.k, self.v, bt, cl, ks, vs, new[2],
+                                                      None, max_context_len)
+                else:
+                    ops.paged_attention_fp8_v2(out, self.exp_sums[:S], self.max_logits[:S], self.tmp_out[:S], q,
+                                               self.k, self.v, bt, cl, ks, vs, None, max_context_len)
+                self.launches_per_step = 2 + extra
             return
         if max_context_len <= V1_MAX_CONTEXT:
             if new is None:

@@ -167,10 +167,11 @@ def paged_attention_v2(out, exp_sums, max_logits, tmp_output, query, key_cache, 
 
 def _check_new_rows(key, value, query, key_cache):
     want = (query.shape[0], key_cache.shape[1], key_cache.shape[3])
+    dt = query.dtype if key_cache.dtype == torch.float8_e4m3fn else key_cache.dtype
     for name, t in (("key", key), ("value", value)):
-        if tuple(t.shape) != want or t.dtype != key_cache.dtype or not t.is_contiguous():
+        if tuple(t.shape) != want or t.dtype != dt or not t.is_contiguous():
             raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT,
-                                 f"{name} must be contiguous {key_cache.dtype} of shape {want}")
+                                 f"{name} must be contiguous {dt} of shape {want}")
 
 
 def paged_attention_append_v1(out, query, key, value, key_cache, value_cache, block_tables, context_lens,
@@ -257,6 +258,51 @@ def paged_attention_fp8_v2(out, exp_sums, max_logits, tmp_output, query, key_cac
     check(lib.cf_paged_attention_fp8_v2(ctypes.byref(p), float(k_scale), float(v_scale), _ptr(exp_sums),
                                         _ptr(max_logits), _ptr(tmp_output), exp_sums.shape[-1], _stream(query)),
           "cf_paged_attention_fp8_v2")
+    return out
+
+
+def paged_attention_fp8_append_v1(out, query, key, value, key_cache, value_cache, block_tables, context_lens,
+                                  k_scale, v_scale, slot_mapping=None, scale=None, max_context_len=None,
+                                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused decode step over float8_e4m3fn caches: reshape_and_cache_fp8 of
+    every row's newest token (key/value of the query dtype) followed by
+    paged_attention_fp8_v1, in one launch (rules as paged_attention_append_v1)."""
+    lib = _lib.load()
+    _check_new_rows(key, value, query, key_cache)
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len, fp8=True)
+    ws = _ptr(workspace)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib.cf_paged_attention_fp8_append_v1(ctypes.byref(p), float(k_scale), float(v_scale), _ptr(key),
+                                               _ptr(value), _ptr(slot_mapping), ws, ws_bytes, _stream(query)),
+          "cf_paged_attention_fp8_append_v1")
+    return out
+
+
+def paged_attention_fp8_append_v2(out, exp_sums, max_logits, tmp_output, query, key, value, key_cache,
+                                  value_cache, block_tables, context_lens, k_scale, v_scale, slot_mapping=None,
+                                  scale=None, max_context_len=None) -> torch.Tensor:
+    """Partitioned form of paged_attention_fp8_append_v1 (scratch as paged_attention_v2)."""
+    lib = _lib.load()
+    _check_new_rows(key, value, query, key_cache)
+    if scale is None:
+        scale = 1.0 / math.sqrt(query.shape[-1])
+    if max_context_len is None:
+        max_context_len = int(context_lens.max().item()) if context_lens.numel() else 0
+    p = _attention_params(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                          max_context_len, fp8=True)
+    for t in (exp_sums, max_logits, tmp_output):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise CacheFlowError(_lib.CF_ERR_INVALID_ARGUMENT, "v2 scratch must be contiguous float32")
+    check(lib.cf_paged_attention_fp8_append_v2(ctypes.byref(p), float(k_scale), float(v_scale), _ptr(key),
+                                               _ptr(value), _ptr(slot_mapping), _ptr(exp_sums),
+                                               _ptr(max_logits), _ptr(tmp_output), exp_sums.shape[-1],
+                                               _stream(query)),
+          "cf_paged_attention_fp8_append_v2")
     return out
 
 

@@ -165,6 +165,27 @@ CF_API cf_status cf_paged_attention_fp8_v2(const cf_paged_attention_params* para
                                            float* max_logits, float* tmp_output,
                                            int32_t num_partitions, void* stream);
 
+/* Fused decode step over fp8 caches: cf_reshape_and_cache_fp8(key, value, ...,
+ * slot_mapping, num_tokens = num_seqs, k_scale, v_scale) followed by
+ * cf_paged_attention_fp8_v1, in one launch.  Same rules as
+ * cf_paged_attention_append_v1 (row s appends at position context_lens[s] - 1;
+ * key / value [num_seqs, num_kv_heads, head_dim] of params->dtype, 16-byte
+ * aligned) and the same stored bytes as cf_reshape_and_cache_fp8. */
+CF_API cf_status cf_paged_attention_fp8_append_v1(const cf_paged_attention_params* params,
+                                                  float k_scale, float v_scale, const void* key,
+                                                  const void* value, const int32_t* slot_mapping,
+                                                  void* workspace, size_t workspace_bytes,
+                                                  void* stream);
+
+/* Partitioned form of cf_paged_attention_fp8_append_v1 (scratch as
+ * cf_paged_attention_v2). */
+CF_API cf_status cf_paged_attention_fp8_append_v2(const cf_paged_attention_params* params,
+                                                  float k_scale, float v_scale, const void* key,
+                                                  const void* value, const int32_t* slot_mapping,
+                                                  float* exp_sums, float* max_logits,
+                                                  float* tmp_output, int32_t num_partitions,
+                                                  void* stream);
+
 /* cf_reshape_and_cache into fp8 (e4m3) caches: key/value rows of `dtype`
  * (CF_F32, CF_F16 or CF_BF16) are stored as e4m3(x / scale) -- x / scale
  * rounded to f32, then to the nearest e4m3 (ties to even), saturating at

@@ -128,6 +128,13 @@ def test_invalid_arguments_rejected_without_gpu(cflib):
     p.num_blocks = 64
     assert cflib.cf_paged_attention_append_v2(ctypes.byref(p), 1 << 20, 1 << 20, None, es, es, es, 1, None) == \
         _lib.CF_ERR_WORKSPACE
+    # fused fp8 append: scales finite and > 0, rows present, then the v2 scratch rules
+    assert cflib.cf_paged_attention_fp8_append_v2(ctypes.byref(p), 0.0, 1.0, 1 << 20, 1 << 20, None, es, es, es, 1,
+                                                  None) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_paged_attention_fp8_append_v1(ctypes.byref(p), 1.0, 1.0, None, 1 << 20, None, None, 0,
+                                                  None) == _lib.CF_ERR_INVALID_ARGUMENT
+    assert cflib.cf_paged_attention_fp8_append_v2(ctypes.byref(p), 0.5, 1.0, 1 << 20, 1 << 20, None, es, es, es, 1,
+                                                  None) == _lib.CF_ERR_WORKSPACE
     # scheduler block ops: ids are range-checked on the host before anything runs
     pairs = (ctypes.c_int64 * 2)(0, 5)
     assert cflib.cf_execute_block_ops(None, None, None, None, 4096, 4, 4, None, 0, None, 0, None, 0, None) == _lib.CF_OK

@@ -71,7 +71,8 @@ def test_engine_steps_fused_and_separate(cflib, oracle_mod, dtype, H, Hkv, D, ct
     ("f16", 8, 8, 128, [1, 17, 300, 2000]),
     ("bf16", 32, 8, 128, [5, 16, 9000, 700]),
 ])
-def test_engine_steps_fp8_caches(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+@pytest.mark.parametrize("fused", [False, True])
+def test_engine_steps_fp8_caches(cflib, oracle_mod, dtype, H, Hkv, D, ctx, fused):
     import torch
 
     from cacheflow_b200.engine import DecodeEngine
@@ -86,7 +87,7 @@ def test_engine_steps_fp8_caches(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
     dk = torch.from_numpy(k.copy()).cuda().view(torch.float8_e4m3fn)
     dv = torch.from_numpy(v.copy()).cuda().view(torch.float8_e4m3fn)
     tdt = torch.float16 if dtype == "f16" else torch.bfloat16
-    eng = DecodeEngine(dk, dv, H, S, tables.shape[1], S, kv_scales=(ks, vs), query_dtype=tdt)
+    eng = DecodeEngine(dk, dv, H, S, tables.shape[1], S, kv_scales=(ks, vs), query_dtype=tdt, fused_append=fused)
     outs = []
     steps_in = []
     for i in range(steps):

@@ -1,7 +1,9 @@
 """FP8 (e4m3) KV caches: the quantizing scatter (cf_reshape_and_cache_fp8) is
-bit-exact against the oracle's rounding, and decode attention over fp8 caches
+bit-exact against the oracle's rounding, decode attention over fp8 caches
 (cf_paged_attention_fp8_v1/_v2, FMA and tensor-core consumers) matches the
-oracle's attention over the dequantized caches within the 16-bit tolerance."""
+oracle's attention over the dequantized caches within the 16-bit tolerance,
+and the fused fp8 decode step (cf_paged_attention_fp8_append_v1/_v2) equals
+the scatter followed by the attention bit for bit."""
 
 import math
 
@@ -107,6 +109,115 @@ def test_fp8_attention_matches_oracle(cflib, oracle_mod, consumer, path, dtype, 
                                           num_threads=8)
     assert_close(as_f64(out), want, dtype, f"fp8 attention {path}")
     assert ops.device_errors(0) == 0
+
+
+APPEND_CASES = [
+    ("f16", 8, 8, 128, [1, 15, 16, 17, 513, 3000]),
+    ("bf16", 32, 8, 128, [1, 2, 16, 17, 1025, 4000]),
+    ("bf16", 32, 2, 128, [3, 160, 1030]),
+    ("f16", 16, 2, 256, [1, 17, 1500]),
+]
+
+
+@pytest.mark.parametrize("path", ["v1", "v1_split", "v2"])
+@pytest.mark.parametrize("dtype,H,Hkv,D,ctx", APPEND_CASES)
+def test_fp8_append_equals_reshape_then_attention(cflib, oracle_mod, consumer, path, dtype, H, Hkv, D, ctx):
+    """cf_paged_attention_fp8_append_v1/_v2 store the same e4m3 bytes as
+    cf_reshape_and_cache_fp8 and return the same output, bit for bit, as
+    that scatter followed by cf_paged_attention_fp8_v1/_v2."""
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(hash(("fp8_append", dtype, H, Hkv, D, len(ctx), path)) % 2**32)
+    S = len(ctx)
+    pool = sum((c + 15) // 16 for c in ctx) + 5
+    tables = random_tables(rng, ctx, pool)
+    cl = np.array(ctx, np.int32)
+    pos = cl - 1
+    slots = (tables[np.arange(S), pos // 16] * 16 + pos % 16).astype(np.int32)
+    q = host_values((S, H, D), dtype, 0.5, rng)
+    nk = host_values((S, Hkv, D), dtype, 20.0, rng)    # past 448 * K_SCALE: saturates
+    nv = host_values((S, Hkv, D), dtype, 0.02, rng)    # subnormal codes
+    kc, vc = _fp8_cache(rng, (pool, Hkv, 16, D)), _fp8_cache(rng, (pool, Hkv, 16, D))
+    dq, dnk, dnv = to_dev(q, dtype), to_dev(nk, dtype), to_dev(nv, dtype)
+    bt, dcl, dsl = to_dev(tables), to_dev(cl), to_dev(slots)
+    mctx = int(cl.max())
+
+    def run(fused, with_slots):
+        dk, dv = _to_fp8_dev(kc), _to_fp8_dev(vc)
+        out = torch.full((S, H, D), 3.0, dtype=torch_dtype(dtype), device="cuda")
+        sl = dsl if with_slots else None
+        if not fused:
+            ops.reshape_and_cache_fp8(dnk, dnv, dk, dv, dsl, K_SCALE, V_SCALE)
+        if path == "v2":
+            P = ops.v2_num_partitions(mctx)
+            es = torch.empty((S, H, P), device="cuda")
+            ml = torch.empty_like(es)
+            to = torch.empty((S, H, P, D), device="cuda")
+            if fused:
+                ops.paged_attention_fp8_append_v2(out, es, ml, to, dq, dnk, dnv, dk, dv, bt, dcl, K_SCALE, V_SCALE,
+                                                  sl)
+            else:
+                ops.paged_attention_fp8_v2(out, es, ml, to, dq, dk, dv, bt, dcl, K_SCALE, V_SCALE)
+        else:
+            ws = None
+            if path == "v1_split":
+                n = ops.paged_attention_v1_workspace_size(dq, dk, bt, mctx)
+                ws = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda") if n else None
+            if fused:
+                ops.paged_attention_fp8_append_v1(out, dq, dnk, dnv, dk, dv, bt, dcl, K_SCALE, V_SCALE, sl,
+                                                  workspace=ws)
+            else:
+                ops.paged_attention_fp8_v1(out, dq, dk, dv, bt, dcl, K_SCALE, V_SCALE, workspace=ws)
+        return out, dk.view(torch.uint8), dv.view(torch.uint8)
+
+    ops.device_errors(0, clear=True)
+    o_ref, k_ref, v_ref = run(False, True)
+    for with_slots in (False, True):
+        o, kk, vv = run(True, with_slots)
+        assert torch.equal(kk, k_ref) and torch.equal(vv, v_ref), "fp8 cache after the fused append"
+        assert torch.equal(o, o_ref), "fused fp8 output differs from reshape_and_cache_fp8 + attention"
+    assert ops.device_errors(0) == 0
+    k2, v2 = kc.copy(), vc.copy()
+    oracle_mod.reshape_and_cache_fp8(nk, nv, k2, v2, slots, K_SCALE, V_SCALE, CODE[dtype])
+    assert np.array_equal(k_ref.cpu().numpy(), k2) and np.array_equal(v_ref.cpu().numpy(), v2)
+    want = oracle_mod.paged_attention_fp8(q, k2, v2, tables, cl, 1 / math.sqrt(D), K_SCALE, V_SCALE, CODE[dtype],
+                                          num_threads=8)
+    assert_close(as_f64(o_ref), want, dtype, f"fp8 append {path}")
+
+
+def test_fp8_append_wrong_slot_appends_nothing(cflib, oracle_mod):
+    import torch
+
+    from cacheflow_b200 import _lib, ops
+
+    rng = np.random.default_rng(16)
+    ctx = [20, 33, 700, 64]
+    tables = random_tables(rng, ctx, 60)
+    cl = np.array(ctx, np.int32)
+    pos = cl - 1
+    slots = (tables[np.arange(4), pos // 16] * 16 + pos % 16).astype(np.int32)
+    bad = slots.copy()
+    bad[1] = -1
+    bad[2] = slots[2] + 1
+    q = host_values((4, 32, 128), "bf16", 0.5, rng)
+    nk = host_values((4, 8, 128), "bf16", 0.5, rng)
+    nv = host_values((4, 8, 128), "bf16", 0.5, rng)
+    kc, vc = _fp8_cache(rng, (60, 8, 16, 128)), _fp8_cache(rng, (60, 8, 16, 128))
+    dk, dv = _to_fp8_dev(kc), _to_fp8_dev(vc)
+    out = torch.empty((4, 32, 128), dtype=torch.bfloat16, device="cuda")
+    ops.device_errors(0, clear=True)
+    ops.paged_attention_fp8_append_v1(out, to_dev(q, "bf16"), to_dev(nk, "bf16"), to_dev(nv, "bf16"), dk, dv,
+                                      to_dev(tables), to_dev(cl), K_SCALE, V_SCALE, to_dev(bad))
+    assert ops.device_errors(0, clear=True) == _lib.CF_DEVERR_SLOT
+    ok = np.array([True, False, False, True])
+    k2, v2 = kc.copy(), vc.copy()
+    oracle_mod.reshape_and_cache_fp8(nk[ok], nv[ok], k2, v2, slots[ok], K_SCALE, V_SCALE, CODE["bf16"])
+    assert np.array_equal(dk.view(torch.uint8).cpu().numpy(), k2)
+    assert np.array_equal(dv.view(torch.uint8).cpu().numpy(), v2)
+    want = oracle_mod.paged_attention_fp8(q, k2, v2, tables, cl, 1 / math.sqrt(128), K_SCALE, V_SCALE, CODE["bf16"])
+    assert_close(as_f64(out), want, "bf16", "rows that append nothing attend to the cache as it is")
 
 
 def test_fp8_nan_codes_past_context_do_not_leak(cflib, oracle_mod, consumer):
