@@ -274,7 +274,7 @@ def run_ours(args):
     nc = len(w.chunk_context_lens) if chunked else 0
     # decode-only batches (one new token per row, at its newest position)
     # append it inside the attention launch unless --append separate
-    fused = args.append == "fused" and not w.has_chunks and T == S
+    fused = (args.append == "fused" or (args.append == "auto" and not fp8)) and not w.has_chunks and T == S
     new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
                           max_chunks=nc, fused_append=fused, kv_scales=(kv_scale, kv_scale) if fp8 else None,
@@ -631,9 +631,10 @@ def main():
                     help="small batches: read a clean buffer after the L2-flush write")
     ap.add_argument("--kv-dtype", choices=["native", "fp8"], default="native",
                     help="KV cache element type: the workload's own, or fp8 e4m3 with a per-cache scale")
-    ap.add_argument("--append", choices=["fused", "separate"], default="fused",
+    ap.add_argument("--append", choices=["auto", "fused", "separate"], default="auto",
                     help="decode batches: append the new K/V inside the attention launch, or run "
-                         "reshape_and_cache before it")
+                         "reshape_and_cache before it (auto: fused for 16-bit caches, separate for fp8, "
+                         "the faster of the two on each)")
     ap.add_argument("--prefill", choices=["chunked", "rows"], default="chunked",
                     help="prefill tokens of mixed batches: multi-query chunks or one decode row each")
     ap.add_argument("--swap-gb", type=float, default=4.0, help="GB swapped out and in (whole job)")
