@@ -220,6 +220,44 @@ def test_fp8_append_wrong_slot_appends_nothing(cflib, oracle_mod):
     assert_close(as_f64(out), want, "bf16", "rows that append nothing attend to the cache as it is")
 
 
+@pytest.mark.parametrize("path", ["v1", "v2"])
+def test_fp8_attention_wide_score_range(cflib, oracle_mod, path):
+    """Scores spanning ~40 (log2 units) in random block order: the running
+    reference point both moves (by more than the lazy threshold) and stays
+    put while blocks below it are added."""
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng(17)
+    ctx = [3000, 700, 16, 5000]
+    S, H, Hkv, D = len(ctx), 32, 8, 128
+    pool = sum((c + 15) // 16 for c in ctx) + 3
+    tables = random_tables(rng, ctx, pool)
+    cl = np.array(ctx, np.int32)
+    q = host_values((S, H, D), "bf16", 0.5, rng)
+    ramp = (0.05 + 4.0 * rng.random(pool) ** 2).astype(np.float32)[:, None, None, None]
+    x = torch.from_numpy(rng.standard_normal((pool, Hkv, 16, D)).astype(np.float32) * 2 * ramp)
+    kc = x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    vc = _fp8_cache(rng, (pool, Hkv, 16, D))
+    ks, vs = 1.0, 0.1
+    dq, dk, dv = to_dev(q, "bf16"), _to_fp8_dev(kc), _to_fp8_dev(vc)
+    bt, dcl = to_dev(tables), to_dev(cl)
+    out = torch.empty((S, H, D), dtype=torch.bfloat16, device="cuda")
+    if path == "v2":
+        P = ops.v2_num_partitions(int(cl.max()))
+        es = torch.empty((S, H, P), device="cuda")
+        ml = torch.empty_like(es)
+        to = torch.empty((S, H, P, D), device="cuda")
+        ops.paged_attention_fp8_v2(out, es, ml, to, dq, dk, dv, bt, dcl, ks, vs)
+    else:
+        ops.paged_attention_fp8_v1(out, dq, dk, dv, bt, dcl, ks, vs)
+    want = oracle_mod.paged_attention_fp8(q, kc, vc, tables, cl, 1 / math.sqrt(D), ks, vs, CODE["bf16"],
+                                          num_threads=8)
+    assert_close(as_f64(out), want, "bf16", f"fp8 attention, wide score range, {path}")
+    assert ops.device_errors(0) == 0
+
+
 def test_fp8_nan_codes_past_context_do_not_leak(cflib, oracle_mod, consumer):
     import torch
 
