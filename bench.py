@@ -277,6 +277,7 @@ def run_ours(args):
     fused = (args.append == "fused" or (args.append == "auto" and not fp8)) and not w.has_chunks and T == S
     new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
+                          kernel=args.kernel,
                           max_chunks=nc, fused_append=fused, kv_scales=(kv_scale, kv_scale) if fp8 else None,
                           query_dtype=tdt)
     engine.q[:S].copy_(q)
@@ -459,7 +460,9 @@ def run_ours(args):
                 "prefill": ("chunked: %d decode rows + %d chunks through the multi-query operator"
                             % (chunks[0], chunks[1]) if chunked else
                             ("one decode row per prefill token" if w.has_chunks else None)),
-                "attention": "v1" if mctx <= 8192 else "v2",
+                "attention": ("v2 (512-token partitions)" if engine._use_v2(mctx) else
+                              "v1" + (" (split into partitions, merged by a reduce kernel)"
+                                      if engine.workspace is not None else "")),
                 "v1_split": args.v1_split,
                 "append": ("new K/V appended inside the attention launch" if fused
                            else "reshape_and_cache launch before attention"),
@@ -481,7 +484,7 @@ def run_ours(args):
             "frac_of_hbm_peak": round(value / (peak * world), 4),
             "roofline": {
                 "bound": "hbm",
-                "kernel": ("paged_attention" + ("_v1" if mctx <= 8192 else "_v2+reduce")
+                "kernel": ("paged_attention" + ("_v2+reduce" if engine._use_v2(mctx) else "_v1")
                            + ("+paged_prefill" if chunked else "")),
                 "achieved": round(achieved, 1),
                 "peak": peak,
@@ -623,6 +626,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama2_7b_ragged_decode", choices=sorted(workloads.WORKLOADS))
     ap.add_argument("--v1-split", choices=["on", "off"], default="on")
+    ap.add_argument("--kernel", choices=["v1", "reference"], default="v1",
+                    help="decode attention: v1 with the library's context split at every length, or the "
+                         "reference's choice (v1 up to 8192 tokens, v2 with 512-token partitions beyond)")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

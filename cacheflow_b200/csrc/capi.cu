@@ -31,11 +31,12 @@ namespace {
 
 constexpr int32_t kV2PartitionTokens = 512;  // CacheFlow's PARTITION_SIZE (paged_attention.cu:368)
 
-// Tokens per partition of the split path of cf_paged_attention_v1: 1024, or
-// 512 when that is needed to give the grid about four CTAs per SM of a B200
-// (148 SMs).  Shorter partitions do not pay: below ~512 tokens the extra
-// reduce launch costs more than the added parallelism.  0 disables splitting;
-// CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never) overrides the choice.
+// Tokens per partition of the split path of cf_paged_attention_v1 (policy
+// below).  Shorter partitions do not pay: below ~512 tokens the extra reduce
+// launch costs more than the added parallelism (the fp32 8-sequence batch
+// steps in 34 us at 128- or 256-token partitions against 29 us unsplit).
+// 0 disables splitting; CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never)
+// overrides the choice.
 int32_t v1_split_tokens(const cf_paged_attention_params* p) {
   static const int32_t forced = [] {
     if (const char* e = std::getenv("CF_V1_SPLIT_TOKENS")) {
@@ -45,9 +46,13 @@ int32_t v1_split_tokens(const cf_paged_attention_params* p) {
     return (int32_t)-1;
   }();
   if (forced >= 0) return forced;
+  // 1024-token partitions, or 2048 past 8192 tokens (a long context then
+  // writes and merges a quarter of the partial results of v2's 512-token
+  // partitions: 0.589 vs 0.639 ms on 16 rows of 16K-128K tokens), halved
+  // down to 512 while that is needed for about four CTAs per SM.
   constexpr int64_t kTargetCtas = 4 * 148;
   const int64_t pairs = (int64_t)p->num_seqs * p->num_kv_heads;
-  int32_t split = 1024;
+  int32_t split = p->max_context_len > 8192 ? 2048 : 1024;
   while (split > 512 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
   return split;
 }

@@ -7,9 +7,12 @@ memory (prepare_kv_cache_inputs, :92-131) and hands those host pointers, a
 null query and a null output to the attention launcher (:137-176).  Here the
 same host-side batch description is staged into device buffers owned by the
 engine, the new K/V rows are scattered into the cache, attention runs on the
-device, and the output is copied back.  The kernel choice follows the
-reference: v1 when the longest context is at most 8192 tokens, else v2 with
-512-token partitions (:162-177).
+device, and the output is copied back.  Attention runs v1 with the
+library's own context split for every length (kernel="v1", the default:
+2048-token partitions past 8192 tokens write a quarter of v2's partial
+results), or follows the reference's choice (kernel="reference": v1 when the
+longest context is at most 8192 tokens, else v2 with 512-token partitions,
+:162-177).
 
 Steps are pipelined over `depth` staging slots and three streams: the
 host-to-device copies of step i+1 and the device-to-host copy of step i-1
@@ -50,7 +53,7 @@ class DecodeEngine:
                  max_seqs: int, max_blocks_per_seq: int, max_new_tokens: int | None = None,
                  stream: torch.cuda.Stream | None = None, split_v1: bool = True, depth: int = 2,
                  max_chunks: int = 0, fused_append: bool = False, kv_scales: tuple[float, float] | None = None,
-                 query_dtype: torch.dtype | None = None):
+                 query_dtype: torch.dtype | None = None, kernel: str = "v1"):
         """kv_scales = (k_scale, v_scale) with float8_e4m3fn caches: the caches
         hold K / k_scale and V / v_scale; queries, new K/V rows and outputs are
         `query_dtype` (f16 / bf16)."""
@@ -78,13 +81,18 @@ class DecodeEngine:
         s0 = self.slots_[0]
         self.q, self.out, self.tables, self.ctx = s0.q, s0.out, s0.tables, s0.ctx
         max_ctx = max_blocks_per_seq * self.block_size
+        if kernel not in ("v1", "reference"):
+            raise ValueError("kernel must be 'v1' or 'reference'")
+        # contexts longer than this run v2 (None: never)
+        self.v2_above = V1_MAX_CONTEXT if kernel == "reference" else None
         self.workspace = None
         if split_v1:
-            n = ops.paged_attention_v1_workspace_size(self.q, key_cache, self.tables, min(max_ctx, V1_MAX_CONTEXT))
+            v1_ctx = max_ctx if self.v2_above is None else min(max_ctx, self.v2_above)
+            n = ops.paged_attention_v1_workspace_size(self.q, key_cache, self.tables, v1_ctx)
             if n:
                 self.workspace = torch.empty((n,), dtype=torch.uint8, device=dev)
         self.parts = ops.v2_num_partitions(max_ctx)
-        if max_ctx > V1_MAX_CONTEXT:
+        if self.v2_above is not None and max_ctx > self.v2_above:
             self.exp_sums = torch.empty((max_seqs, num_heads, self.parts), dtype=torch.float32, device=dev)
             self.max_logits = torch.empty_like(self.exp_sums)
             self.tmp_out = torch.empty((max_seqs, num_heads, self.parts, self.head_dim), dtype=torch.float32,
@@ -103,6 +111,9 @@ class DecodeEngine:
     def d2h_bytes(self, num_seqs: int) -> int:
         return num_seqs * self.num_heads * self.head_dim * self.q.element_size()
 
+    def _use_v2(self, max_context_len: int) -> bool:
+        return self.v2_above is not None and max_context_len > self.v2_above
+
     def _attend(self, q, out, bt, cl, num_seqs: int, max_context_len: int, new=None) -> None:
         """new = (k_new, v_new, slot_mapping) of one token per row appends it
         in the same launch."""
@@ -113,7 +124,7 @@ class DecodeEngine:
             if new is not None and not fused:
                 ops.reshape_and_cache_fp8(new[0], new[1], self.k, self.v, new[2], ks, vs)
             extra = 1 if new is not None and not fused else 0
-            if max_context_len <= V1_MAX_CONTEXT:
+            if not self._use_v2(max_context_len):
                 if fused:
                     ops.paged_attention_fp8_append_v1(out, q, new[0], new[1], self.k, self.v, bt, cl, ks, vs, new[2],
                                                       None, max_context_len, workspace=self.workspace)
@@ -133,7 +144,7 @@ class DecodeEngine:
                                                self.k, self.v, bt, cl, ks, vs, None, max_context_len)
                 self.launches_per_step = 2 + extra
             return
-        if max_context_len <= V1_MAX_CONTEXT:
+        if not self._use_v2(max_context_len):
             if new is None:
                 ops.paged_attention_v1(out, q, self.k, self.v, bt, cl, None, max_context_len,
                                        workspace=self.workspace)
