@@ -186,3 +186,30 @@ def test_v1_workspace_size_needs_shapes_only(cflib):
     assert n >= rows * (128 + 2) * 4
     p.max_context_len = 1000  # fits one partition: never splits
     assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == 0
+
+
+def _split_bytes(rows, D):
+    r = lambda b: (b + 255) // 256 * 256
+    return 2 * r(rows * 4) + r(rows * D * 4)
+
+
+def test_v1_split_policy(cflib):
+    """Partitions of 1024 tokens, 2048 past 8192 tokens, halved (not below
+    512) while the grid would hold fewer than ~4 CTAs per SM of 148."""
+    import os
+
+    from cacheflow_b200 import _lib
+
+    if os.environ.get("CF_V1_SPLIT_TOKENS"):
+        pytest.skip("CF_V1_SPLIT_TOKENS overrides the policy")
+    p = _lib.AttentionParams()
+    p.num_heads, p.head_dim, p.block_size, p.dtype = 32, 128, 16, _lib.CF_BF16
+    # 16 rows x 8 kv heads up to 124,872 tokens: 2048-token partitions (61)
+    p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 16, 8, 124872, 7805
+    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(16 * 32 * 61, 128)
+    # 64 rows x 32 kv heads up to 4096 tokens: 1024-token partitions (4)
+    p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 64, 32, 4096, 256
+    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(64 * 32 * 4, 128)
+    # 2 rows x 8 kv heads up to 20,000 tokens: 2048 gives 160 CTAs, 1024 320, 512 640
+    p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 2, 8, 20000, 1250
+    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(2 * 32 * 40, 128)

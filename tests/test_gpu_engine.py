@@ -13,11 +13,12 @@ from helpers import CODE, as_f64, assert_close, random_tables, to_dev, to_host
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("kernel", ["v1", "reference"])
 @pytest.mark.parametrize("dtype,H,Hkv,D,ctx", [
     ("f16", 8, 8, 128, [1, 17, 300, 2000]),
-    ("bf16", 32, 8, 128, [5, 16, 9000, 700]),   # longest > 8192: the v2 path
+    ("bf16", 32, 8, 128, [5, 16, 9000, 700]),   # longest > 8192: v1 split at 2048, or v2 ("reference")
 ])
-def test_engine_steps_fused_and_separate(cflib, oracle_mod, dtype, H, Hkv, D, ctx):
+def test_engine_steps_fused_and_separate(cflib, oracle_mod, dtype, H, Hkv, D, ctx, kernel):
     import torch
 
     from cacheflow_b200.engine import DecodeEngine
@@ -35,7 +36,8 @@ def test_engine_steps_fused_and_separate(cflib, oracle_mod, dtype, H, Hkv, D, ct
     results = {}
     for fused in (False, True):
         dk, dv = to_dev(k0, dtype), to_dev(v0, dtype)
-        eng = DecodeEngine(dk, dv, H, S, tables.shape[1], S, fused_append=fused, depth=2)
+        eng = DecodeEngine(dk, dv, H, S, tables.shape[1], S, fused_append=fused, depth=2, kernel=kernel)
+        assert eng._use_v2(max(ctx) + steps) == (kernel == "reference" and max(ctx) > 8192)
         outs = []
         pins = []
         for i in range(steps):
