@@ -413,8 +413,9 @@ struct TcLayout {
   static constexpr int kStage = 2 * kKBytes;          // K, then V
   static constexpr int kRingOff = kTcTiles * kQBytes;
   static constexpr int kBarOff = kRingOff + kTcStages * kStage;
-  // kv_full, kv_empty per stage; s_full, p_full, o_done per tile; fin
-  static constexpr int kNumBars = 2 * kTcStages + 3 * kTcTiles + 1;
+  // kv_full, kv_empty per stage; s_full per tile and S buffer; p_full,
+  // o_done per tile; fin
+  static constexpr int kNumBars = 2 * kTcStages + 4 * kTcTiles + 1;
   static constexpr int kMaskOff = kBarOff + kNumBars * 8;
   static constexpr int kTmemOff = kMaskOff + kTcStages * 4;
   static constexpr int kBytes = kTmemOff + 16;
@@ -460,8 +461,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + kTcStages;
-  uint64_t* s_full = bars + 2 * kTcStages;  // per tile
-  uint64_t* p_full = s_full + kTcTiles;     // per tile
+  uint64_t* s_full = bars + 2 * kTcStages;  // per tile and S buffer: [2 x + buf]
+  uint64_t* p_full = s_full + 2 * kTcTiles; // per tile
   uint64_t* o_done = p_full + kTcTiles;     // per tile
   uint64_t* fin = o_done + kTcTiles;
   int* vmask = reinterpret_cast<int*>(smem + L::kMaskOff);
@@ -475,7 +476,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(smem_addr(&kv_empty[s]), 1);
     }
     for (int x = 0; x < kTcTiles; ++x) {
-      mbar_init(smem_addr(&s_full[x]), 1);
+      mbar_init(smem_addr(&s_full[2 * x]), 1);
+      mbar_init(smem_addr(&s_full[2 * x + 1]), 1);
       mbar_init(smem_addr(&p_full[x]), 4 * 32);
       mbar_init(smem_addr(&o_done[x]), 1);
     }
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t bd = smem_desc_sw128(kb + (kk >> 2) * L::kKVBox + (kk & 3) * 32, 16, 1024);
           tc_mma_f16(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        tc_commit(smem_addr(&s_full[x]));
+        tc_commit(smem_addr(&s_full[2 * x + (st & 1)]));
       };
       auto issue_pv = [&](int st, int x) {
         const uint32_t vb =
@@ -604,17 +606,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_commit(smem_addr(&o_done[x]));
       };
-      if (mbar_wait_bounded(smem_addr(&kv_full[0]), 0)) {
+      // S is double-buffered per tile, so a tile's QK runs two stages ahead:
+      // QK(st + 2) follows PV(st) (it overwrites the buffer P(st) was read
+      // from, in issue order) and is done long before the tile's softmax
+      // finishes stage st + 1, which therefore never waits for the tensor
+      // pipe's round trip.
+      auto wait_kv = [&](int st) {
+        const bool r = mbar_wait_bounded(smem_addr(&kv_full[st % kTcStages]), (uint32_t)(st / kTcStages) & 1u);
         tc_fence_after();
-        issue_qk(0, 0);
-        issue_qk(0, 1);
-      } else {
-        ok = false;
+        return r;
+      };
+      for (int st = 0; ok && st < 2 && st < nstages; ++st) {
+        if (!wait_kv(st)) {
+          ok = false;
+          break;
+        }
+        issue_qk(st, 0);
+        issue_qk(st, 1);
       }
       for (int st = 0; ok && st < nstages; ++st) {
-        const bool next = st + 1 < nstages;
+        const bool ahead = st + 2 < nstages;
         for (int x = 0; x < kTcTiles; ++x) {
-          // P of this tile written (and its S read): PV, then the next S.
+          // P of this tile written (and its S read): PV, then the S two
+          // stages on.
           if (!mbar_wait_bounded(smem_addr(&p_full[x]), (uint32_t)st & 1u)) {
             ok = false;
             break;
@@ -623,16 +637,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           issue_pv(st, x);
           // after the last tile's PV this stage's K/V may be refilled
           if (x == kTcTiles - 1) tc_commit(smem_addr(&kv_empty[st % kTcStages]));
-          if (next) {
-            if (x == 0) {
-              if (!mbar_wait_bounded(smem_addr(&kv_full[(st + 1) % kTcStages]),
-                                     (uint32_t)((st + 1) / kTcStages) & 1u)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+          if (ahead) {
+            if (x == 0 && !wait_kv(st + 2)) {
+              ok = false;
+              break;
             }
-            issue_qk(st + 1, x);
+            issue_qk(st + 2, x);
           }
         }
       }
@@ -655,7 +665,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     for (int st = 0; st < nstages; ++st) {
       const int slot = st % kTcStages;
-      const bool r1 = mbar_wait_bounded(smem_addr(&s_full[x]), (uint32_t)st & 1u);
+      const bool r1 = mbar_wait_bounded(smem_addr(&s_full[2 * x + (st & 1)]), (uint32_t)(st >> 1) & 1u);
       const bool r2 = mbar_wait_bounded(smem_addr(&kv_full[slot]), (uint32_t)(st / kTcStages) & 1u);
       if (!__all_sync(0xffffffffu, r1 && r2)) {
         ok = false;
