@@ -376,9 +376,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 // (16-bit head in its first 32 columns, remainder in the next 32: K-major A
 // operands in tensor memory); then O += P_hi V + P_lo V with A read from
 // tensor memory and V an MN-major B operand in shared memory.
-// The MMA warp alternates the tiles -- PV_A(s), QK_A(s+1), PV_B(s),
-// QK_B(s+1) -- so one tile's softmax runs while the tensor core works for
-// the other, and every K/V byte brought in feeds 256 query rows.  O is
+// The MMA warp alternates the tiles -- PV_A(s), QK_A(s+2), PV_B(s),
+// QK_B(s+2): each tile's QK runs two stages ahead on its two S buffers, so
+// its softmax finds the next S ready -- and every K/V byte brought in feeds
+// 256 query rows.  O is
 // rescaled (tcgen05.ld / st) only when a row's max grows by more than 2^8:
 // until then P may exceed 1 by at most 2^8, which f32 accumulation absorbs.
 // K and V tiles are placed box-major ([64-column box][4 blocks][16 rows]
