@@ -366,7 +366,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 // its MMAs) that share every K/V stage, and 10 warps:
 //   warps 0-3  softmax + epilogue of tile A, warps 4-7 of tile B: thread =
 //              row = tensor-memory lane (warp w reads lanes 32 (w % 4) ..);
-//   warp 8     TMA producer (64-key stages of K and V, 3-stage ring);
+//   warp 8     TMA producer (64-key stages of K and V, 5-stage ring);
 //   warp 9     tensor-memory owner and MMA issuer (one thread).
 // Tensor memory (512 columns), per tile: S double-buffered at [0, 64) and
 // [64, 128), O at [128, 128 + D); tile B at +256.
