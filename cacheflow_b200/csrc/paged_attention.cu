@@ -1179,9 +1179,11 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
   return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_reduce_kernel<T, D>, r));
 }
 
-// Which consumer runs: tensor cores for GQA groups of 3+ query heads on 16-bit
-// caches and for every group on fp8 caches (head_dim a multiple of 128), FMA
-// otherwise.
+// Which consumer runs: tensor cores for every group on fp8 caches (head_dim a
+// multiple of 128) and on 16-bit caches for GQA groups of 3+ query heads or
+// head_dim 128 (there the tensor-core consumer is ~1 % faster than FMA even
+// for one query head per KV head: 0.345 vs 0.348 ms on 64 rows of 128-4096
+// tokens, 0.360 vs 0.365 ms under the power cap), FMA otherwise.
 // CF_ATTN_CONSUMER=fma|mma overrides (read per call).
 bool use_mma(const cf_paged_attention_params& p, int64_t rows, bool fp8) {
   if (p.dtype == CF_F32 || p.num_blocks <= 0 || rows > INT32_MAX) return false;
@@ -1191,7 +1193,7 @@ bool use_mma(const cf_paged_attention_params& p, int64_t rows, bool fp8) {
     if (std::strcmp(e, "mma") == 0) return true;
   }
   // fp8 tiles cost the FMA consumer more conversion work than HBM time.
-  return fp8 || p.num_heads / p.num_kv_heads >= 3;
+  return fp8 || p.num_heads / p.num_kv_heads >= 3 || p.head_dim == 128;
 }
 
 template <typename T, typename TC, int D, bool kAppend>
