@@ -434,6 +434,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr uint32_t kAB = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdescQK = tc_idesc_f16(kAB, 0, kTcRows, kTcStageKeys);
   constexpr uint32_t kIdescPV = tc_idesc_f16(kAB, 1, kTcRows, D);
+  // P as a 16-bit head plus remainder (bf16), or a single f16 (f16 inputs)
+  constexpr bool kSplitP = !std::is_same<T, __half>::value;
   constexpr int kBoxBytes = kPBlock * 128;  // one block's 16 rows of one box
 
   const int tile = blockIdx.x;
@@ -600,7 +602,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int j = 0; j < kStageBlocks; ++j) {
 #pragma unroll
-          for (int hl = 0; hl < 2; ++hl) {
+          for (int hl = 0; hl < (kSplitP ? 2 : 1); ++hl) {
             const uint64_t bd = smem_desc_sw128(vb + j * kBoxBytes, L::kKVBox, 1024);
             tc_mma_f16_ts(d, pt + hl * (kTcSCols / 2) + j * 8, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
           }
@@ -752,13 +754,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       // P (16-bit head and remainder) over this stage's S buffer: keys
-      // 2c, 2c+1 in column c (head) and column 32 + c (remainder).
-      {
+      // 2c, 2c+1 in column c (head) and column 32 + c (remainder).  An f16 P
+      // (P <= 2^8, 11 significant bits) needs no remainder.
+      if constexpr (kSplitP) {
         uint32_t hi[kTcStageKeys / 2], lo[kTcStageKeys / 2];
 #pragma unroll
         for (int c = 0; c < kTcStageKeys / 2; ++c) split2<T>(s[2 * c], s[2 * c + 1], hi[c], lo[c]);
         tmem_st32(trow + (st & 1) * kTcSCols, reinterpret_cast<float(&)[32]>(hi));
         tmem_st32(trow + (st & 1) * kTcSCols + 32, reinterpret_cast<float(&)[32]>(lo));
+        tmem_wait_st();
+      } else {
+        uint32_t hi[kTcStageKeys / 2];
+#pragma unroll
+        for (int c = 0; c < kTcStageKeys / 2; ++c) hi[c] = pack2<T>(s[2 * c], s[2 * c + 1]);
+        tmem_st32(trow + (st & 1) * kTcSCols, reinterpret_cast<float(&)[32]>(hi));
         tmem_wait_st();
       }
       // V rows the MMA must not multiply (not loaded this stage, past the

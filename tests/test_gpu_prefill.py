@@ -62,6 +62,7 @@ CASES = [
     ("bf16", 8, 8, 128, [(0, 100), (4000, 129), (15, 2)]),
     ("bf16", 16, 2, 128, [(7, 70), (1500, 33)]),
     ("f16", 12, 4, 64, [(0, 45), (900, 200)]),  # group of 3: 21 tokens per tile
+    ("f16", 8, 8, 128, [(0, 100), (15, 2), (4000, 129)]),  # f16 P without a remainder: short rows too
     ("bf16", 64, 1, 64, [(50, 9), (0, 3)]),     # group of 64: one token per tile
 ]
 
