@@ -56,7 +56,11 @@ class DecodeEngine:
                  query_dtype: torch.dtype | None = None, kernel: str = "v1"):
         """kv_scales = (k_scale, v_scale) with float8_e4m3fn caches: the caches
         hold K / k_scale and V / v_scale; queries, new K/V rows and outputs are
-        `query_dtype` (f16 / bf16)."""
+        `query_dtype` (f16 / bf16).  kernel = "v1" (v1 with the library's
+        split at every context length) or "reference" (v1 up to 8192 tokens,
+        v2 beyond, as CacheFlow's engine chooses)."""
+        if kernel not in ("v1", "reference"):
+            raise ValueError("kernel must be 'v1' or 'reference'")
         self.k = key_cache
         self.v = value_cache
         self.device = key_cache.device
@@ -81,8 +85,6 @@ class DecodeEngine:
         s0 = self.slots_[0]
         self.q, self.out, self.tables, self.ctx = s0.q, s0.out, s0.tables, s0.ctx
         max_ctx = max_blocks_per_seq * self.block_size
-        if kernel not in ("v1", "reference"):
-            raise ValueError("kernel must be 'v1' or 'reference'")
         # contexts longer than this run v2 (None: never)
         self.v2_above = V1_MAX_CONTEXT if kernel == "reference" else None
         self.workspace = None

@@ -213,3 +213,12 @@ def test_v1_split_policy(cflib):
     # 2 rows x 8 kv heads up to 20,000 tokens: 2048 gives 160 CTAs, 1024 320, 512 640
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 2, 8, 20000, 1250
     assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(2 * 32 * 40, 128)
+
+
+def test_engine_rejects_unknown_kernel_choice_before_touching_a_gpu():
+    import torch
+
+    from cacheflow_b200.engine import DecodeEngine
+
+    with pytest.raises(ValueError):
+        DecodeEngine(torch.empty((4, 2, 16, 64)), torch.empty((4, 2, 16, 64)), 2, 1, 1, kernel="v3")
