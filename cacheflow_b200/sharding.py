@@ -19,7 +19,9 @@ block_manager.cpp:35-79), partitioned per GPU.
 
 from __future__ import annotations
 
+import copy
 import heapq
+import time
 from dataclasses import dataclass, field
 from typing import Callable
 
@@ -133,7 +135,9 @@ def gather_blocks_cuda(cache, ids: list[int], out) -> None:
 
     from . import ops
 
-    m = torch.tensor([[b, i] for i, b in enumerate(ids)], dtype=torch.int64, device=cache.device)
+    if not ids:
+        return
+    m = torch.tensor([[b, i] for i, b in enumerate(ids)], dtype=torch.int64).to(cache.device, non_blocking=True)
     ops.swap_blocks(cache, out, m, stream_tensor=cache)
 
 
@@ -143,42 +147,167 @@ def scatter_blocks_cuda(buf, cache, ids: list[int]) -> None:
 
     from . import ops
 
-    m = torch.tensor([[i, b] for i, b in enumerate(ids)], dtype=torch.int64, device=cache.device)
+    if not ids:
+        return
+    m = torch.tensor([[i, b] for i, b in enumerate(ids)], dtype=torch.int64).to(cache.device, non_blocking=True)
     ops.swap_blocks(buf, cache, m, stream_tensor=cache)
 
 
-def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
-            gather: Callable = gather_blocks_cuda, scatter: Callable = scatter_blocks_cuda) -> None:
-    """Executes rebalance moves with point-to-point sends (every rank calls this
-    with the same `moves`; `pools` is every rank's bookkeeping, kept in sync).
+class MigrationError(RuntimeError):
+    """A migration's transfers failed on this rank (the peer went away, or the
+    deadline passed).  The transport has been aborted (with NCCL: the
+    communicator, so every later collective on it fails at once instead of
+    hanging), and this rank's pool bookkeeping is unchanged."""
 
-    gather / scatter move blocks between the cache and a contiguous staging
+
+class MigrationTimeout(MigrationError):
+    """The transfers of a migration did not finish before its deadline."""
+
+
+class P2PTransport:
+    """Point-to-point transfers through torch.distributed: NCCL send/recv over
+    NVLink between GPUs, gloo between CPU processes.  Every transfer of one
+    migration is posted in a single batch_isend_irecv group."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def start(self, sends, recvs) -> list:
+        """sends / recvs: lists of (tensor, peer rank).  Returns handles."""
+        import torch.distributed as dist
+
+        ops = [dist.P2POp(dist.isend, t, peer, self.group) for t, peer in sends]
+        ops += [dist.P2POp(dist.irecv, t, peer, self.group) for t, peer in recvs]
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    def wait(self, handles, timeout_s: float, poll_s: float = 2e-4) -> None:
+        """Waits for every handle until the deadline; on expiry aborts and
+        raises MigrationTimeout.  The host never blocks without a bound inside
+        the communication library, so a peer that died or never sends cannot
+        hang it.  NCCL handles are polled (is_completed() follows the device);
+        gloo handles report completion only from wait(), which takes the
+        remaining time as its own limit."""
+        import datetime
+
+        import torch.distributed as dist
+
+        deadline = time.monotonic() + timeout_s
+        if dist.get_backend(self.group) == "gloo":
+            for i, h in enumerate(handles):
+                left = deadline - time.monotonic()
+                try:
+                    if left <= 0:
+                        raise RuntimeError("deadline passed")
+                    h.wait(datetime.timedelta(seconds=left))
+                except RuntimeError as e:
+                    self.abort()
+                    if time.monotonic() < deadline - 1e-3 and "deadline" not in str(e) and "imed out" not in str(e):
+                        raise MigrationError(f"transfer {i} of {len(handles)} failed: {e}") from e
+                    raise MigrationTimeout(f"{len(handles) - i} of {len(handles)} transfers unfinished after "
+                                           f"{timeout_s:g} s") from None
+            return
+        pending = list(handles)
+        while pending:
+            try:
+                pending = [h for h in pending if not h.is_completed()]
+            except RuntimeError as e:  # the communicator reported an error
+                self.abort()
+                raise MigrationError(f"transfer failed: {e}") from e
+            if not pending:
+                break
+            if time.monotonic() > deadline:
+                self.abort()
+                raise MigrationTimeout(f"{len(pending)} of {len(handles)} transfers unfinished after {timeout_s:g} s")
+            time.sleep(poll_s)
+        for h in handles:
+            h.wait()  # orders the current CUDA stream after the transfer
+
+    def abort(self) -> None:
+        import torch.distributed as dist
+
+        try:
+            dist.distributed_c10d._abort_process_group(self.group or dist.group.WORLD)
+        except Exception:  # gloo has no abort; the caller tears the group down
+            pass
+
+
+def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
+            gather: Callable = gather_blocks_cuda, scatter: Callable = scatter_blocks_cuda,
+            transport=None, timeout_s: float = 60.0) -> dict:
+    """Executes rebalance moves (seq, src rank, dst rank) with point-to-point
+    transfers.  Every rank calls this with the same `moves`; `pools` is every
+    rank's bookkeeping, kept identical on all ranks.
+
+    A sender gathers the blocks of all its outgoing sequences into one staging
+    buffer per cache (one block-copy launch each, ordered by destination), a
+    receiver gets one contiguous K and one V slice per source, and all
+    transfers of the call go out as one group; nothing synchronises the host
+    with the device in between (NCCL orders its stream after the gather).
+    The host waits for completion with a deadline (`timeout_s`): on expiry the
+    transport is aborted and MigrationTimeout is raised with this rank's
+    bookkeeping unchanged (MigrationError, its base, when a transfer fails
+    before the deadline, e.g. because the peer exited).  On success the receivers scatter the slices into
+    blocks allocated from their own pools and every rank applies the moves to
+    `pools`.  Returns {"blocks_sent", "blocks_received", "bytes_sent",
+    "bytes_received"} for this rank (K and V).
+
+    gather / scatter move blocks between a cache and a contiguous staging
     buffer; the defaults are the library's CUDA kernels.
     """
     import torch
-    import torch.distributed as dist
 
+    transport = transport or P2PTransport()
+    # the new bookkeeping, applied to a copy first: destination ids are
+    # allocated in move order, identically on every rank
+    new = copy.deepcopy(pools)
+    src_ids, dst_ids = {}, {}
     for seq, src, dst in moves:
-        # Bookkeeping is deterministic, so every rank applies it identically.
-        src_ids = list(pools[src].tables[seq])
-        dst_ids = pools[dst].add_sequence(seq, pools[src].lens[seq])
-        pools[src].remove_sequence(seq)
-        shape = (len(src_ids),) + tuple(k_cache.shape[1:])
-        if rank == src:
-            kb = torch.empty(shape, dtype=k_cache.dtype, device=k_cache.device)
-            vb = torch.empty_like(kb)
-            gather(k_cache, src_ids, kb)
-            gather(v_cache, src_ids, vb)
-            if k_cache.is_cuda:
-                torch.cuda.current_stream(k_cache.device).synchronize()
-            reqs = [dist.P2POp(dist.isend, kb, dst), dist.P2POp(dist.isend, vb, dst)]
-            for w in dist.batch_isend_irecv(reqs):
-                w.wait()
-        elif rank == dst:
-            kb = torch.empty(shape, dtype=k_cache.dtype, device=k_cache.device)
-            vb = torch.empty_like(kb)
-            reqs = [dist.P2POp(dist.irecv, kb, src), dist.P2POp(dist.irecv, vb, src)]
-            for w in dist.batch_isend_irecv(reqs):
-                w.wait()
-            scatter(kb, k_cache, dst_ids)
-            scatter(vb, v_cache, dst_ids)
+        src_ids[seq] = list(new[src].tables[seq])
+        dst_ids[seq] = new[dst].add_sequence(seq, new[src].lens[seq])
+        new[src].remove_sequence(seq)
+
+    tail = tuple(k_cache.shape[1:])
+    block_bytes = k_cache[0].numel() * k_cache.element_size()
+    out_moves = sorted((m for m in moves if m[1] == rank and m[2] != rank), key=lambda m: m[2])
+    in_moves = [m for m in moves if m[2] == rank and m[1] != rank]
+    sends, recvs, incoming = [], [], []
+    n_out = sum(len(src_ids[s]) for s, _, _ in out_moves)
+    if n_out:
+        ids = [b for s, _, _ in out_moves for b in src_ids[s]]
+        kb = torch.empty((n_out,) + tail, dtype=k_cache.dtype, device=k_cache.device)
+        vb = torch.empty_like(kb)
+        gather(k_cache, ids, kb)
+        gather(v_cache, ids, vb)
+        o = 0
+        for peer in sorted({m[2] for m in out_moves}):
+            n = sum(len(src_ids[s]) for s, _, d in out_moves if d == peer)
+            sends += [(kb[o:o + n], peer), (vb[o:o + n], peer)]
+            o += n
+    for peer in sorted({m[1] for m in in_moves}):
+        seqs = [s for s, src, _ in in_moves if src == peer]
+        n = sum(len(src_ids[s]) for s in seqs)
+        kr = torch.empty((n,) + tail, dtype=k_cache.dtype, device=k_cache.device)
+        vr = torch.empty_like(kr)
+        recvs += [(kr, peer), (vr, peer)]
+        incoming.append((kr, vr, [b for s in seqs for b in dst_ids[s]]))
+    try:
+        handles = transport.start(sends, recvs)
+    except RuntimeError as e:  # e.g. the peer aborted or exited already
+        transport.abort()
+        raise MigrationError(f"posting the transfers failed: {e}") from e
+    transport.wait(handles, timeout_s)
+    for kr, vr, ids in incoming:
+        scatter(kr, k_cache, ids)
+        scatter(vr, v_cache, ids)
+    # local moves (src == dst) need no transfer: copy block by block
+    for seq, src, dst in moves:
+        if src == dst == rank:
+            for cache in (k_cache, v_cache):
+                tmp = torch.empty((len(src_ids[seq]),) + tail, dtype=cache.dtype, device=cache.device)
+                gather(cache, src_ids[seq], tmp)
+                scatter(tmp, cache, dst_ids[seq])
+    for p, q in zip(pools, new):
+        p.__dict__.update(q.__dict__)
+    n_in = sum(len(ids) for _, _, ids in incoming)
+    return {"blocks_sent": n_out, "blocks_received": n_in, "bytes_sent": 2 * n_out * block_bytes,
+            "bytes_received": 2 * n_in * block_bytes}

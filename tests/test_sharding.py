@@ -2,8 +2,10 @@
 pools, rebalance planning, and block migration between two gloo ranks on CPU
 (the CUDA block-copy kernels are swapped for CPU gathers here only)."""
 
+import copy
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -85,29 +87,33 @@ def _migration_worker(rank, world, port, result_dir):
     g = torch.Generator().manual_seed(100 + rank)
     k = torch.randn(shape, generator=g)
     v = torch.randn(shape, generator=g)
-    before = {s: (k[pools[rank].tables[s]].clone(), v[pools[rank].tables[s]].clone()) for s in pools[rank].tables}
     loads = [p.load() for p in pools]
     src = int(np.argmax(loads))
     dst = 1 - src
+    # both directions in one call: the largest sequence of the loaded rank
+    # one way, the smallest of the other rank back
     seq = max(pools[src].tables, key=lambda s: pools[src].lens[s])
-    moves = [(seq, src, dst)]
-    sent = None
-    if rank == src:
-        sent = (k[pools[src].tables[seq]].clone(), v[pools[src].tables[seq]].clone())
-    sharding.migrate(moves, rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter)
-    if rank == src:
-        torch.save(sent, os.path.join(result_dir, "sent.pt"))
+    back = min(pools[dst].tables, key=lambda s: pools[dst].lens[s])
+    moves = [(seq, src, dst), (back, dst, src)]
+    stay = [s for s in pools[rank].tables if s not in (seq, back)]
+    before = {s: (k[pools[rank].tables[s]].clone(), v[pools[rank].tables[s]].clone()) for s in stay}
+    mine = seq if rank == src else back
+    torch.save((k[pools[rank].tables[mine]].clone(), v[pools[rank].tables[mine]].clone()),
+               os.path.join(result_dir, f"sent{rank}.pt"))
+    stats = sharding.migrate(moves, rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter, timeout_s=60)
     dist.barrier()
-    if rank == dst:
-        sk, sv = torch.load(os.path.join(result_dir, "sent.pt"))
-        ids = pools[dst].tables[seq]
-        ok = torch.equal(k[ids], sk) and torch.equal(v[ids], sv)
-        # untouched sequences keep their blocks
-        for s, (bk, bv) in before.items():
-            ok = ok and torch.equal(k[pools[dst].tables[s]], bk) and torch.equal(v[pools[dst].tables[s]], bv)
-        with open(os.path.join(result_dir, "ok"), "w") as f:
-            f.write("1" if ok else "0")
-    assert seq not in pools[src].tables and seq in pools[dst].tables
+    got = back if rank == src else seq
+    sk, sv = torch.load(os.path.join(result_dir, f"sent{1 - rank}.pt"))
+    ids = pools[rank].tables[got]
+    ok = torch.equal(k[ids], sk) and torch.equal(v[ids], sv)
+    # untouched sequences keep their blocks
+    for s, (bk, bv) in before.items():
+        ok = ok and torch.equal(k[pools[rank].tables[s]], bk) and torch.equal(v[pools[rank].tables[s]], bv)
+    ok = ok and stats["blocks_received"] == len(ids) and stats["bytes_received"] == 2 * len(ids) * k[0].numel() * 4
+    ok = ok and seq in pools[dst].tables and seq not in pools[src].tables
+    ok = ok and back in pools[src].tables and back not in pools[dst].tables
+    with open(os.path.join(result_dir, f"ok{rank}"), "w") as f:
+        f.write("1" if ok else "0")
     dist.barrier()
     dist.destroy_process_group()
 
@@ -117,4 +123,105 @@ def test_block_migration_two_gloo_ranks(tmp_path):
 
     port = _free_port()
     mp.start_processes(_migration_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
-    assert (tmp_path / "ok").read_text() == "1"
+    assert (tmp_path / "ok0").read_text() == "1"
+    assert (tmp_path / "ok1").read_text() == "1"
+
+
+class _DropSecondSend(sharding.P2PTransport):
+    """Posts only the first of its sends: the V slice is lost on the way."""
+
+    def start(self, sends, recvs):
+        return super().start(sends[:1], recvs)
+
+
+class _DelaySends(sharding.P2PTransport):
+    """Posts its sends only after `delay` seconds."""
+
+    def __init__(self, delay):
+        super().__init__()
+        self.delay = delay
+
+    def start(self, sends, recvs):
+        if sends:
+            time.sleep(self.delay)
+        return super().start(sends, recvs)
+
+
+def _faulty_migration_worker(rank, world, port, result_dir, mode, delay, timeout_s):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ctx = np.array([300, 50, 700, 20, 400, 90], np.int64)
+    pools = sharding.shard_workload(ctx, world, pool_factor=3.0, rng=np.random.default_rng(5))
+    shape = (max(p.num_blocks for p in pools) + 64, 2, 16, 8)
+    k = torch.randn(shape, generator=torch.Generator().manual_seed(100 + rank))
+    v = torch.randn_like(k)
+    src = int(np.argmax([p.load() for p in pools]))
+    dst = 1 - src
+    seq = max(pools[src].tables, key=lambda s: pools[src].lens[s])
+    snapshot = copy.deepcopy(pools)
+    transport = sharding.P2PTransport()
+    if rank == src:
+        transport = _DropSecondSend() if mode == "drop" else _DelaySends(delay)
+    t0 = time.monotonic()
+    try:
+        sharding.migrate([(seq, src, dst)], rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter,
+                         transport=transport, timeout_s=timeout_s if rank == dst else 60.0)
+        outcome = "ok"
+    except sharding.MigrationTimeout:
+        outcome = "timeout"
+    except sharding.MigrationError:
+        outcome = "error"
+    elapsed = time.monotonic() - t0
+    unchanged = all(a.tables == b.tables and a.free == b.free for a, b in zip(pools, snapshot))
+    with open(os.path.join(result_dir, f"r{rank}"), "w") as f:
+        f.write(f"{outcome} {elapsed:.3f} {int(unchanged)} {int(rank == dst)}")
+    # each rank stays up until the other has its result, so no transfer meets
+    # a peer that has exited; both then leave without a group teardown (the
+    # receiver's abandoned receive is still posted)
+    flag = os.path.join(result_dir, f"r{1 - rank}")
+    t1 = time.monotonic()
+    while not os.path.exists(flag) and time.monotonic() - t1 < 60:
+        time.sleep(0.05)
+    os._exit(0)
+
+
+def _run_faulty(tmp_path, mode, delay, timeout_s):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_faulty_migration_worker, args=(2, _free_port(), str(tmp_path), mode, delay, timeout_s),
+                       nprocs=2, start_method="spawn")
+    res = {}
+    for r in (0, 1):
+        outcome, elapsed, unchanged, is_dst = (tmp_path / f"r{r}").read_text().split()
+        res["dst" if is_dst == "1" else "src"] = (outcome, float(elapsed), unchanged == "1")
+    return res
+
+
+def test_migration_dropped_transfer_times_out(tmp_path):
+    """The sender loses its V slice: the receiver's wait ends at the deadline
+    with MigrationTimeout and leaves its bookkeeping untouched."""
+    res = _run_faulty(tmp_path, "drop", 0.0, 1.5)
+    outcome, elapsed, unchanged = res["dst"]
+    assert outcome == "timeout"
+    assert 1.5 <= elapsed < 15
+    assert unchanged
+
+
+def test_migration_late_transfer_times_out(tmp_path):
+    """The sender posts 6 s late, past the receiver's 1.5 s deadline: the
+    receiver raises at its deadline, not when the data finally comes."""
+    res = _run_faulty(tmp_path, "delay", 6.0, 1.5)
+    outcome, elapsed, unchanged = res["dst"]
+    assert outcome == "timeout"
+    assert 1.5 <= elapsed < 5.5
+    assert unchanged
+
+
+def test_migration_late_transfer_within_deadline_completes(tmp_path):
+    res = _run_faulty(tmp_path, "delay", 0.5, 20.0)
+    assert res["dst"][0] == "ok" and not res["dst"][2]
+    assert res["src"][0] == "ok"
