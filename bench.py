@@ -63,7 +63,7 @@ def hbm_peak():
 
 
 # ---------------------------------------------------------------------------
-# Clock sampling during the timed region (nvidia-smi, 100 ms period).
+# Clock sampling during the timed region (nvidia-smi, 50 ms period).
 # ---------------------------------------------------------------------------
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,clocks_event_reasons.active,"
@@ -78,7 +78,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -171,6 +171,9 @@ def time_pool_ops(w, k_cache, v_cache, world: int, swap_gb: float):
       swap_out / swap_in  swap_gb / world GB of K blocks to / from pinned host
                           memory with the SM copy kernel (cf_swap_blocks);
       swap_out_dma        the same through the copy engines (cf_swap_blocks_dma);
+      block_ops_swap_out / block_ops_swap_in
+                          the same bytes as K and V pairs through
+                          cf_execute_block_ops (host pair lists);
       compact             compaction of the pool after half of its sequences
                           are freed (cf_compaction_plan + cf_compact_kv_cache).
     """
@@ -210,7 +213,21 @@ def time_pool_ops(w, k_cache, v_cache, world: int, swap_gb: float):
     ms = timed(lambda: ops.swap_blocks_dma(k_cache, host, host_map, stream_tensor=k_cache), reps=1)
     res["swap_out_dma"] = {"bytes": nbytes, "ms": round(ms, 3), "GB/s": round(nbytes / ms / 1e6, 1),
                            "note": "random block ids: one copy per block"}
-    del host
+    # the scheduler's form of the same traffic: n/2 scattered (GPU, CPU) pairs
+    # of K and V blocks through cf_execute_block_ops (host pair lists)
+    h = n // 2
+    hk, hv = host[:h], host[h:2 * h]
+    so = np.ascontiguousarray(np.stack([ids[:h], np.arange(h)], 1))
+    si = np.ascontiguousarray(np.stack([np.arange(h), ids[:h]], 1))
+    ms = timed(lambda: ops.execute_block_ops(k_cache, v_cache, hk, hv, swaps_out=so))
+    res["block_ops_swap_out"] = {"bytes": 2 * h * block_bytes, "ms": round(ms, 3),
+                                 "GB/s": round(2 * h * block_bytes / ms / 1e6, 1),
+                                 "note": "cf_execute_block_ops, K and V, random block ids"}
+    ms = timed(lambda: ops.execute_block_ops(k_cache, v_cache, hk, hv, swaps_in=si))
+    res["block_ops_swap_in"] = {"bytes": 2 * h * block_bytes, "ms": round(ms, 3),
+                                "GB/s": round(2 * h * block_bytes / ms / 1e6, 1),
+                                "note": "cf_execute_block_ops, K and V, random block ids"}
+    del host, hk, hv
     keep = rng.random(w.num_seqs) < 0.5
     used = np.zeros(w.num_blocks, np.uint8)
     for s in np.flatnonzero(keep):
@@ -224,23 +241,21 @@ def time_pool_ops(w, k_cache, v_cache, world: int, swap_gb: float):
     return res
 
 
-def run_ours(args):
+def measure(args, w, rank: int, world: int, dev, kernel: str, steps: int, warmup: int, e2e: bool = True,
+            post=None) -> dict:
+    """Times `steps` decode steps of workload `w` on this rank (after `warmup`
+    untimed ones) and, with e2e, the same step through DecodeEngine.step from
+    pinned host buffers.  Every timed attention launch is bracketed by CUDA
+    events on the engine's stream.  post(k_cache, v_cache) runs after the
+    timings with the caches still resident and its result is returned as
+    "post".  Collectives: barriers only (the caller all-reduces)."""
     import torch
     import torch.distributed as dist
 
-    from cacheflow_b200 import _lib, ops
+    from cacheflow_b200 import ops
     from cacheflow_b200.engine import DecodeEngine
 
-    rank, world, local = dist_env()
-    _lib.load()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    w, scaling = rank_workload(args, rank, world)
+    local = dev.index
     tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[w.dtype]
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
@@ -276,9 +291,8 @@ def run_ours(args):
     fused = (args.append == "fused" or (args.append == "auto" and not fp8)) and not w.has_chunks and T == S
     new_rows = (k_new, v_new, slots) if fused else None
     engine = DecodeEngine(k_cache, v_cache, H, S, w.block_tables.shape[1], T, split_v1=(args.v1_split == "on"),
-                          kernel=args.kernel,
-                          max_chunks=nc, fused_append=fused, kv_scales=(kv_scale, kv_scale) if fp8 else None,
-                          query_dtype=tdt)
+                          kernel=kernel, max_chunks=nc, fused_append=fused,
+                          kv_scales=(kv_scale, kv_scale) if fp8 else None, query_dtype=tdt)
     engine.q[:S].copy_(q)
     engine.tables.copy_(tables)
     engine.ctx.copy_(ctx)
@@ -325,9 +339,8 @@ def run_ours(args):
         else:
             engine.attend(S, mctx, chunks, new_rows)
 
-    launches_per_step = None
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step()
         launches_per_step = engine.launches_per_step + (0 if fused else 1) + (1 if pairs is not None else 0)
         torch.cuda.synchronize(dev)
@@ -339,6 +352,10 @@ def run_ours(args):
         if clocks:
             clocks.start()
             time.sleep(0.25)
+        # the GPU idled while the sampler started: bring its clocks back up
+        # with a few more untimed steps before the timed region
+        for _ in range(3):
+            step()
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
@@ -346,7 +363,7 @@ def run_ours(args):
         t1 = torch.cuda.Event(enable_timing=True)
         step_ev = []
         t0.record(stream)
-        for i in range(args.steps):
+        for i in range(steps):
             if flush is not None:
                 # the batch fits in L2: overwrite L2 before every step and time
                 # the steps alone
@@ -359,9 +376,8 @@ def run_ours(args):
                 b.record(stream)
                 step_ev.append((a, b))
             else:
-                # the attention launch of every 8th step (and the last) is
-                # bracketed by events for the kernel's own duration
-                step(record=(i % 8 == 0 or i == args.steps - 1))
+                # every timed attention launch is bracketed by its own events
+                step(record=True)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
@@ -370,45 +386,242 @@ def run_ours(args):
     if flush is not None:
         ms_step = sum(a.elapsed_time(b) for a, b in step_ev) / len(step_ev)
     else:
-        ms_step = t0.elapsed_time(t1) / args.steps
+        ms_step = t0.elapsed_time(t1) / steps
     att_ms = sum(a.elapsed_time(b) for a, b in att_ev) / len(att_ev)
-
-    # e2e through the public engine API with pinned host buffers.
-    nrows = chunks[0] if chunked else S  # rows described by block tables / context lengths
-    pin = dict(
-        q=q.cpu().pin_memory(), k=k_new.cpu().pin_memory(), v=v_new.cpu().pin_memory(),
-        s=slots.cpu().pin_memory(), t=tables[:nrows].cpu().pin_memory(), c=ctx[:nrows].cpu().pin_memory(),
-        o=torch.empty((S, H, D), dtype=tdt).pin_memory())
-    chunks_host = None
-    if chunked:
-        chunks_host = (chunks[0], torch.from_numpy(w.chunk_query_start).pin_memory(),
-                       torch.from_numpy(w.chunk_context_lens).pin_memory(),
-                       torch.from_numpy(w.chunk_block_tables).pin_memory())
-    for _ in range(max(3, args.warmup // 4)):
-        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
-    engine.synchronize()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    engine.h2d.wait_event(e0)  # the copy streams start inside the timed region too
-    engine.d2h.wait_event(e0)
-    e2e_steps = max(1, args.steps // 2)
-    for _ in range(e2e_steps):
-        engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
-    engine.join()  # the last output copy ends the region
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
     if ops.device_errors(local) != 0:
         raise RuntimeError("device error word set during the timed region")
 
-    pool_ops = None
-    if args.workload in SHARDED and not args.no_pool_ops and not fp8:
+    e2e_ms = None
+    if e2e:
+        # e2e through the public engine API with pinned host buffers.
+        nrows = chunks[0] if chunked else S  # rows described by block tables / context lengths
+        pin = dict(
+            q=q.cpu().pin_memory(), k=k_new.cpu().pin_memory(), v=v_new.cpu().pin_memory(),
+            s=slots.cpu().pin_memory(), t=tables[:nrows].cpu().pin_memory(), c=ctx[:nrows].cpu().pin_memory(),
+            o=torch.empty((S, H, D), dtype=tdt).pin_memory())
+        chunks_host = None
+        if chunked:
+            chunks_host = (chunks[0], torch.from_numpy(w.chunk_query_start).pin_memory(),
+                           torch.from_numpy(w.chunk_context_lens).pin_memory(),
+                           torch.from_numpy(w.chunk_block_tables).pin_memory())
+        for _ in range(max(3, warmup // 4)):
+            engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
+        engine.synchronize()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        engine.h2d.wait_event(e0)  # the copy streams start inside the timed region too
+        engine.d2h.wait_event(e0)
+        e2e_steps = max(1, steps // 2)
+        for _ in range(e2e_steps):
+            engine.step(pin["q"], pin["k"], pin["v"], pin["s"], pin["t"], pin["c"], pin["o"], mctx, chunks_host)
+        engine.join()  # the last output copy ends the region
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        if ops.device_errors(local) != 0:
+            raise RuntimeError("device error word set during the end-to-end region")
+
+    alg_bytes = kv_step + w.qo_bytes() + w.table_bytes()
+    if fused:  # the appended rows: new K/V read, cache rows written, slots read
+        alg_bytes += 2 * T * Hkv * D * (k_new.element_size() + k_cache.element_size()) + 4 * T
+    res = {
+        "ms_step": ms_step, "att_ms": att_ms, "e2e_ms": e2e_ms, "kv_step": kv_step, "alg_bytes": alg_bytes,
+        "launches_per_step": launches_per_step, "clocks": clock_info, "fused": fused, "fp8": fp8,
+        "kv_scale": kv_scale, "chunked": chunked, "chunks": chunks, "flush": flush is not None,
+        "flush_clean": flush_clean is not None, "v2": engine._use_v2(mctx), "split": engine.workspace is not None,
+        "attention_launches": len(att_ev),
+        "h2d_bytes": engine.h2d_bytes(S, T), "d2h_bytes": engine.d2h_bytes(S),
+    }
+    if post is not None:
         with torch.cuda.stream(stream):
-            pool_ops = time_pool_ops(w, k_cache, v_cache, world, args.swap_gb)
+            res["post"] = post(k_cache, v_cache)
+    del engine, k_cache, v_cache, flush, flush_clean
+    torch.cuda.empty_cache()
+    return res
+
+
+def attention_kind(r: dict) -> str:
+    if r["v2"]:
+        return "v2 (512-token partitions) + reduce"
+    return "v1" + (" (split into partitions, merged by a reduce kernel)" if r["split"] else "")
+
+
+def side_config(args, name: str, rank: int, world: int, dev, peak: float) -> dict:
+    """One more workload timed at N=1 beside the headline, once with the
+    library's v1 split and once with the reference's kernel choice."""
+    w = workloads.make(name, seed=1234)
+    out = {"workload": name, "num_seqs": w.num_seqs, "num_heads": w.num_heads, "num_kv_heads": w.num_kv_heads,
+           "head_dim": w.head_dim, "dtype": w.dtype,
+           "context_lens": "min %d / mean %.0f / max %d" % (w.context_lens.min(), w.context_lens.mean(),
+                                                             w.context_lens.max())}
+    for kernel in ("v1", "reference"):
+        r = measure(args, w, rank, world, dev, kernel, args.steps, args.warmup, e2e=False)
+        if r["att_ms"] > r["ms_step"] * 1.0001:
+            raise RuntimeError(f"{name}: attention time {r['att_ms']} ms above the step time {r['ms_step']} ms")
+        achieved = r["alg_bytes"] / (r["att_ms"] * 1e-3) / 1e9
+        out["v1_split" if kernel == "v1" else "reference_kernel"] = {
+            "attention": attention_kind(r),
+            "value": round(r["kv_step"] / (r["ms_step"] * 1e-3) / 1e9, 1),
+            "unit": UNIT,
+            "ms_per_step": round(r["ms_step"], 4),
+            "kernel_ms": round(r["att_ms"], 4),
+            "achieved": round(achieved, 1),
+            "frac": round(achieved / peak, 4),
+            "alg_bytes_per_launch": r["alg_bytes"],
+            "tokens_per_s": round(w.num_seqs / (r["ms_step"] * 1e-3), 1),
+            "clocks": r["clocks"],
+        }
+    return out
+
+
+def rebalance_check(full, parts, rank: int, world: int, k_cache, v_cache) -> dict:
+    """A rebalancing round after the timed steps (strong-scaled workload, N>1):
+    every rank rebuilds all ranks' pool bookkeeping from the same LPT shares,
+    a seeded fraction of each rank's sequences finishes (rank r loses up to
+    40 % of them, growing with r), plan_rebalance moves sequences from the
+    loaded ranks to the light ones, and migrate() ships their blocks over
+    NCCL.  Timed with CUDA events on this rank's stream (gather -> transfers
+    -> scatter); the caller takes the max over ranks.  Then every moved
+    sequence's attention is computed on its receiver and compared bitwise
+    with what the sender computed before the move."""
+    import torch
+    import torch.distributed as dist
+
+    from cacheflow_b200 import ops, sharding
+
+    dev = k_cache.device
+    pools = []
+    for r in range(world):
+        wr = full.rehome(parts[r], seed=1234 + r)
+        nblk = (wr.context_lens.astype(np.int64) + 15) // 16
+        tabs = {int(g): [int(b) for b in wr.block_tables[i, : nblk[i]]] for i, g in enumerate(parts[r])}
+        used = {b for t in tabs.values() for b in t}
+        free = [b for b in range(wr.num_blocks - 1, -1, -1) if b not in used]
+        pools.append(sharding.LocalPool(wr.num_blocks, free=free, tables=tabs,
+                                        lens={int(g): int(c) for g, c in zip(parts[r], wr.context_lens)}))
+    rng = np.random.default_rng(99)
+    for r, p in enumerate(pools):
+        seqs = sorted(p.tables)
+        frac = 0.4 * r / max(1, world - 1)
+        for s in rng.choice(seqs, int(frac * len(seqs)), replace=False):
+            p.remove_sequence(int(s))
+    loads = [p.load() for p in pools]
+    moves = sharding.plan_rebalance(loads, [p.lens for p in pools], tolerance=0.02)
+    after = list(loads)
+    for s, a, b in moves:
+        c = pools[a].lens[s]
+        after[a] -= c
+        after[b] += c
+
+    def attend(pool, seqs, qq):
+        c, t = pool.block_table(seqs)
+        tt, cc = torch.from_numpy(t).to(dev), torch.from_numpy(c).to(dev)
+        mc = int(c.max())
+        ws = None
+        n = ops.paged_attention_v1_workspace_size(qq, k_cache, tt, mc)
+        if n:
+            ws = torch.empty((n,), dtype=torch.uint8, device=dev)
+        o = torch.empty_like(qq)
+        ops.paged_attention_v1(o, qq, k_cache, v_cache, tt, cc, None, mc, workspace=ws)
+        return o
+
+    H = full.num_heads
+    qdt = k_cache.dtype
+    out_seqs = {}
+    for peer in range(world):
+        seqs = [s for s, a, b in moves if a == rank and b == peer]
+        if seqs:
+            g = torch.Generator(device=dev).manual_seed(777 + rank)
+            qq = torch.empty((len(seqs), H, full.head_dim), dtype=qdt, device=dev).normal_(0, full.std, generator=g)
+            out_seqs[peer] = (seqs, qq, attend(pools[rank], seqs, qq))
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    stats = sharding.migrate(moves, rank, pools, k_cache, v_cache, timeout_s=60.0)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    # verification traffic (not timed): each sender ships the queries and the
+    # outputs it computed; the receiver recomputes on its new blocks
+    sends, recvs, checks = [], [], []
+    for peer, (seqs, qq, oo) in out_seqs.items():
+        sends += [(qq, peer), (oo, peer)]
+    for peer in range(world):
+        seqs = [s for s, a, b in moves if a == peer and b == rank]
+        if seqs:
+            qq = torch.empty((len(seqs), H, full.head_dim), dtype=qdt, device=dev)
+            oo = torch.empty_like(qq)
+            recvs += [(qq, peer), (oo, peer)]
+            checks.append((seqs, qq, oo))
+    tr = sharding.P2PTransport()
+    tr.wait(tr.start(sends, recvs), 60.0)
+    verified = mismatched = 0
+    for seqs, qq, oo in checks:
+        got = attend(pools[rank], seqs, qq)
+        for i in range(len(seqs)):
+            verified += 1
+            mismatched += int(not torch.equal(got[i], oo[i]))
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([ms, stats["bytes_sent"], verified, mismatched, ops.device_errors(dev.index)],
+                     dtype=torch.float64, device=dev)
+    tmax = t[:1].clone()
+    dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    ms_max, sent, verified, mismatched, errs = tmax.item(), t[1].item(), int(t[2].item()), int(t[3].item()), t[4].item()
+    return {
+        "moves": len(moves),
+        "bytes": int(sent),
+        "ms": round(ms_max, 3),
+        "GB/s": round(sent / (ms_max * 1e-3) / 1e9, 1) if ms_max > 0 else None,
+        "load_before": [int(x) for x in loads],
+        "load_after": [int(x) for x in after],
+        "sequences_verified": verified,
+        "bitwise_equal": mismatched == 0 and errs == 0,
+        "how": ("seeded finishes (rank r loses 0.4*r/(N-1) of its sequences), plan_rebalance to 2 %, "
+                "migrate(): block-copy gather, NCCL send/recv into the receiver's HBM, scatter; CUDA events "
+                "gather->scatter, max over ranks; moved sequences' attention recomputed on the receiver"),
+    }
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from cacheflow_b200 import _lib, sharding
+
+    rank, world, local = dist_env()
+    _lib.load()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    w, scaling = rank_workload(args, rank, world)
+    fp8 = args.kv_dtype == "fp8"
+
+    def post(k_cache, v_cache):
+        extra = {}
+        if args.workload in SHARDED and not args.no_pool_ops and not fp8:
+            extra["pool_ops"] = time_pool_ops(w, k_cache, v_cache, world, args.swap_gb)
+        if world > 1 and scaling == "strong" and not args.no_migration and not fp8:
+            full = workloads.make(args.workload, seed=1234, **({"num_seqs": args.num_seqs} if args.num_seqs else {}))
+            parts = sharding.lpt_assign(full.context_lens, world)
+            extra["migration"] = rebalance_check(full, parts, rank, world, k_cache, v_cache)
+        return extra
+
+    r = measure(args, w, rank, world, dev, args.kernel, args.steps, args.warmup, e2e=True, post=post)
+    ms_step, att_ms, e2e_ms = r["ms_step"], r["att_ms"], r["e2e_ms"]
+    if att_ms > ms_step * 1.0001:
+        raise RuntimeError(f"attention time {att_ms} ms above the step time {ms_step} ms")
+    pool_ops = r["post"].get("pool_ops")
+    if pool_ops is not None:
         keys = sorted(pool_ops)
         ms_t = torch.tensor([pool_ops[k]["ms"] for k in keys], dtype=torch.float64, device=dev)
         if world > 1:
@@ -417,6 +630,8 @@ def run_ours(args):
             b = pool_ops[k].get("bytes", pool_ops[k].get("bytes_read_written"))
             pool_ops[k]["all_ranks_GB/s"] = round(world * b / m / 1e6, 1)
 
+    S, H, Hkv, D = w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim
+    kv_step = r["kv_step"]
     times = torch.tensor([ms_step, att_ms, e2e_ms], dtype=torch.float64, device=dev)
     totals = torch.tensor([kv_step, S], dtype=torch.float64, device=dev)
     if world > 1:
@@ -427,11 +642,10 @@ def run_ours(args):
 
     if rank == 0:
         peak, peak_kind = hbm_peak()
-        alg_bytes = kv_step + w.qo_bytes() + w.table_bytes()
-        if fused:  # the appended rows: new K/V read, cache rows written, slots read
-            alg_bytes += 2 * T * Hkv * D * (k_new.element_size() + k_cache.element_size()) + 4 * T
+        alg_bytes = r["alg_bytes"]
         achieved = alg_bytes / (att_ms * 1e-3) / 1e9
         value = kv_total / (ms_step * 1e-3) / 1e9
+        chunks = r["chunks"]
         line = {
             "metric": METRIC,
             "value": round(value, 1),
@@ -448,6 +662,7 @@ def run_ours(args):
             "config": {
                 "workload": w.name,
                 "num_seqs_per_gpu": S,
+                "num_seqs_total": int(seqs_total),
                 "num_heads": H,
                 "num_kv_heads": Hkv,
                 "head_dim": D,
@@ -457,20 +672,19 @@ def run_ours(args):
                 "pool_blocks_per_gpu": w.num_blocks,
                 "kv_bytes_per_step_per_gpu": kv_step,
                 "prefill": ("chunked: %d decode rows + %d chunks through the multi-query operator"
-                            % (chunks[0], chunks[1]) if chunked else
+                            % (chunks[0], chunks[1]) if r["chunked"] else
                             ("one decode row per prefill token" if w.has_chunks else None)),
-                "attention": ("v2 (512-token partitions)" if engine._use_v2(mctx) else
-                              "v1" + (" (split into partitions, merged by a reduce kernel)"
-                                      if engine.workspace is not None else "")),
+                "attention": attention_kind(r),
+                "kernel_choice": args.kernel,
                 "v1_split": args.v1_split,
-                "append": ("new K/V appended inside the attention launch" if fused
+                "append": ("new K/V appended inside the attention launch" if r["fused"]
                            else "reshape_and_cache launch before attention"),
-                "kv_dtype": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % kv_scale
+                "kv_dtype": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % r["kv_scale"]
                              if fp8 else w.dtype),
                 "l2": (("L2 flushed before every timed step (512 MB write, then a 512 MB read of a clean buffer; "
-                        "outside the step's events)" if flush_clean is not None else
+                        "outside the step's events)" if r["flush_clean"] else
                         "L2 flushed before every timed step (512 MB write, outside the step's events)")
-                       if flush is not None else
+                       if r["flush"] else
                        "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (kv_step / 1e9)),
                 "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes() // (w.elem_bytes if fp8 else 1),
                 "parallelism": (f"dp{world} (one global batch, sequences dealt to per-GPU pools by LPT)"
@@ -483,8 +697,8 @@ def run_ours(args):
             "frac_of_hbm_peak": round(value / (peak * world), 4),
             "roofline": {
                 "bound": "hbm",
-                "kernel": ("paged_attention" + ("_v2+reduce" if engine._use_v2(mctx) else "_v1")
-                           + ("+paged_prefill" if chunked else "")),
+                "kernel": ("paged_attention" + ("_v2+reduce" if r["v2"] else "_v1")
+                           + ("+paged_prefill" if r["chunked"] else "")),
                 "achieved": round(achieved, 1),
                 "peak": peak,
                 "unit": "GB/s",
@@ -492,6 +706,7 @@ def run_ours(args):
                 "peak_source": peak_kind,
                 "alg_bytes_per_launch": alg_bytes,
                 "kernel_ms": round(att_ms, 4),
+                "kernel_launches_timed": r["attention_launches"],
                 # the committed captures are of 1-GPU launches: a strong-scaled
                 # rank's launch is another shape
                 "traffic": (traffic_from_profiles(w.name + ("_fp8" if fp8 else ""))
@@ -501,15 +716,21 @@ def run_ours(args):
                 "value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": UNIT,
                 "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": engine.h2d_bytes(S, T),
-                "d2h_bytes_per_step": engine.d2h_bytes(S),
+                "h2d_bytes_per_step": r["h2d_bytes"],
+                "d2h_bytes_per_step": r["d2h_bytes"],
                 "api": "cacheflow_b200.engine.DecodeEngine.step (pinned host in, pinned host out)",
             },
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clock_info,
+            "gpu_launches": r["launches_per_step"] * args.steps,
+            "clocks": r["clocks"],
         }
         if pool_ops is not None:
             line["pool_ops_rank0"] = pool_ops
+        if "migration" in r["post"]:
+            line["migration"] = r["post"]["migration"]
+    if world == 1 and args.side_configs != "none" and not fp8:
+        line["configs"] = {name: side_config(args, name, rank, world, dev, peak)
+                           for name in args.side_configs.split(",") if name != args.workload}
+    if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -547,19 +768,33 @@ def reference_sample(w: workloads.Workload, max_seqs: int):
     return ctx, tables, len(remap)
 
 
-def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | None = None, warmup: int = 1):
+def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | None = None, warmup: int = 1,
+                 max_seqs: int = 16, total_budget_s: float | None = None):
+    """CacheFlow's own CPU decode step on the first rows of `w`.  With
+    `steps`, exactly that many timed steps run; total_budget_s then caps the
+    whole run (warm-up included) by shrinking the sample to fewer rows, found
+    from one probe step of the full sample.  Without `steps`, steps repeat for
+    about budget_s seconds."""
     from oracle import oracle
 
     threads = os.cpu_count() or 1
-    n = min(w.num_seqs, 16)
-    ctx, tables, pool = reference_sample(w, n)
-    ref = oracle.RefCpu(w.num_heads, w.num_kv_heads, w.head_dim, pool, threads)
-    try:
+    n = min(w.num_seqs, max_seqs)
+    while True:
+        ctx, tables, pool = reference_sample(w, n)
+        ref = oracle.RefCpu(w.num_heads, w.num_kv_heads, w.head_dim, pool, threads)
         k, v = ref.caches()
         rng = np.random.default_rng(7)
         k[...] = rng.standard_normal(k.shape, dtype=np.float32) * np.float32(w.std)
         v[...] = rng.standard_normal(v.shape, dtype=np.float32) * np.float32(w.std)
         ref.set_batch(ctx, tables)
+        if steps is None or total_budget_s is None or n == 1:
+            break
+        t_probe = ref.step()
+        if t_probe * (steps + warmup) <= total_budget_s:
+            break
+        ref.close()
+        n = max(1, min(n - 1, int(n * total_budget_s / (t_probe * (steps + warmup)))))
+    try:
         for _ in range(warmup):
             ref.step()
         times = []
@@ -593,8 +828,7 @@ def run_reference(args):
     if rank != 0:
         return
     w = workloads.make(args.workload, seed=1234)
-    cb = cpu_baseline(w, steps=args.steps, warmup=args.warmup)
-    ms = cb["sample"]
+    cb = cpu_baseline(w, steps=args.steps, warmup=args.warmup, total_budget_s=args.cpu_total_seconds)
     line = {
         "metric": METRIC,
         "value": cb["value"],
@@ -604,7 +838,7 @@ def run_reference(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload in SHARDED else "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded N(0,%g))" % w.std,
@@ -623,7 +857,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="llama2_7b_ragged_decode", choices=sorted(workloads.WORKLOADS))
+    ap.add_argument("--workload", default="llama3_70b_sharded", choices=sorted(workloads.WORKLOADS))
+    ap.add_argument("--side-configs", default="llama3_8b_long_decode",
+                    help="comma-separated workloads also timed at N=1 (v1 split and the reference's kernel "
+                         "choice), reported under 'configs'; 'none' to skip")
     ap.add_argument("--v1-split", choices=["on", "off"], default="on")
     ap.add_argument("--kernel", choices=["v1", "reference"], default="v1",
                     help="decode attention: v1 with the library's context split at every length, or the "
@@ -632,6 +869,8 @@ def main():
                     help="override the workload's sequence count (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pool-ops", action="store_true", help="skip swap / compaction timings")
+    ap.add_argument("--no-migration", action="store_true",
+                    help="N>1 strong scaling: skip the rebalancing round (NCCL block migration)")
     ap.add_argument("--l2-clean", choices=["on", "off"], default="on",
                     help="small batches: read a clean buffer after the L2-flush write")
     ap.add_argument("--kv-dtype", choices=["native", "fp8"], default="native",
@@ -644,6 +883,8 @@ def main():
                     help="prefill tokens of mixed batches: multi-query chunks or one decode row each")
     ap.add_argument("--swap-gb", type=float, default=4.0, help="GB swapped out and in (whole job)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-total-seconds", type=float, default=120.0,
+                    help="--impl reference: cap on the whole run; the sample shrinks to fewer rows to fit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

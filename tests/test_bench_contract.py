@@ -22,7 +22,7 @@ def test_reference_arm_prints_one_contract_line():
         assert k in d, k
     assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["warmup"] >= 3
     assert d["value"] > 0 and d["higher_is_better"] is True
-    assert d["config"]["workload"] == "llama2_7b_ragged_decode"
+    assert d["config"]["workload"] == "llama3_70b_sharded" and d["scaling"] == "strong"
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
