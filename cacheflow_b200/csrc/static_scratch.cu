@@ -30,22 +30,29 @@ static __device__ __align__(256) unsigned char g_v2_scratch[kScratchBytes];
 
 size_t round256(size_t b) { return (b + 255) / 256 * 256; }
 
-// Device address of g_v2_scratch on the current device, resolved once per
-// device.  Returns CF_OK and sets *ptr, or the status of the failed lookup.
+// Device address of g_v2_scratch on the current device.  Only a successful
+// lookup is kept: a failed one (for instance out of memory, because with lazy
+// module loading the array is only placed in device memory at this first
+// lookup, or a lookup attempted during stream capture) clears the runtime's
+// error and is tried again on the next call.  Returns CF_OK and sets *ptr,
+// or the status of the failed lookup.
 cf_status scratch_address(void** ptr) {
-  static std::once_flag once[kMaxDevices];
+  static std::mutex mu;
   static void* addr[kMaxDevices];
-  static cudaError_t err[kMaxDevices];
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cfb::cuda_status(e);
   if (dev < 0 || dev >= kMaxDevices) return CF_ERR_UNSUPPORTED;
-  std::call_once(once[dev], [dev] {
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
     void* p = nullptr;
-    err[dev] = cudaGetSymbolAddress(&p, g_v2_scratch);
-    addr[dev] = (err[dev] == cudaSuccess) ? p : nullptr;
-  });
-  if (err[dev] != cudaSuccess) return cfb::cuda_status(err[dev]);
+    e = cudaGetSymbolAddress(&p, g_v2_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // not sticky: leave no error behind for the caller's next call
+      return cfb::cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+    }
+    addr[dev] = p;
+  }
   *ptr = addr[dev];
   return CF_OK;
 }
@@ -57,13 +64,20 @@ extern "C" cf_status cf_paged_attention_v2_static_scratch(const cf_paged_attenti
   if (p == nullptr || p->num_seqs < 0 || p->num_heads <= 0 || p->head_dim <= 0 ||
       p->max_context_len < 0)
     return CF_ERR_INVALID_ARGUMENT;
+  // The shape limits of cf_paged_attention_v2 come first, so the size
+  // arithmetic below works on bounded values only.
+  if (!cfb::attention_supported(p->head_dim, p->block_size, p->dtype)) return CF_ERR_UNSUPPORTED;
+  if (p->num_seqs > 65535 || p->num_heads > 65535) return CF_ERR_UNSUPPORTED;
   const int64_t parts = p->max_context_len > 0
                             ? ((int64_t)p->max_context_len + kPartitionTokens - 1) / kPartitionTokens
                             : 1;
+  // rows < 2^16 * 2^16 * 2^22 = 2^54: no overflow in int64
   const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
+  const int64_t per_row = (int64_t)sizeof(float) * (p->head_dim + 2);
+  if (rows > (int64_t)(kScratchBytes / per_row)) return CF_ERR_WORKSPACE;  // larger than the static area
   const size_t stat_bytes = round256((size_t)rows * sizeof(float));
   const size_t need = 2 * stat_bytes + (size_t)rows * p->head_dim * sizeof(float);
-  if (need > kScratchBytes) return CF_ERR_WORKSPACE;  // larger than the static area
+  if (need > kScratchBytes) return CF_ERR_WORKSPACE;
 
   void* base = nullptr;
   cf_status st = scratch_address(&base);

@@ -250,8 +250,10 @@ typedef struct cf_prefill_params {
 CF_API cf_status cf_paged_prefill_attention(const cf_prefill_params* params, void* stream);
 
 /* Size of the library's built-in scratch for
- * cf_paged_attention_v2_static_scratch: 16 MiB, held on every GPU that loads
- * the library until the process exits. */
+ * cf_paged_attention_v2_static_scratch: 16 MiB of device memory on every GPU
+ * where the entry point has been called, held until the process exits.  With
+ * CUDA's lazy module loading (the default) the array is placed in device
+ * memory by the first call on a device, not when the library loads. */
 #define CF_STATIC_SCRATCH_BYTES (16u << 20)
 
 /* The same computation as cf_paged_attention_v2 for callers that cannot
@@ -266,8 +268,10 @@ CF_API cf_status cf_paged_prefill_attention(const cf_prefill_params* params, voi
  * floats (plus alignment) must fit in CF_STATIC_SCRATCH_BYTES; a larger call
  * returns CF_ERR_WORKSPACE and launches nothing.
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture starts.  All calls share the one array, which
+ * (cudaGetSymbolAddress) with that device current, which can also place the
+ * array in device memory: make that first call before any stream capture
+ * starts and before the host's own pool takes the device's free memory.  A
+ * failed lookup returns its error and is retried by the next call.  All calls share the one array, which
  * keeps the last call's contents (nothing in it needs to start at zero):
  * calls whose kernels overlap on the GPU -- on different streams, or from
  * different threads -- race on it and must be serialised by the caller.
@@ -322,9 +326,14 @@ CF_API cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
  * swap-ins (CPU block -> GPU block), then copy-on-write copies (GPU -> GPU).
  * Each list is HOST int64 [n, 2] of (src, dst) block ids; every id is checked
  * against its pool before anything is enqueued (CF_ERR_INVALID_ARGUMENT).
- * Runs of consecutive ids become single cudaMemcpyAsync calls on the copy
- * engines, so no SM time is used; within one list the pairs apply in order.
- * CPU pools should be pinned for the copies to be asynchronous. */
+ * Within one list the pairs apply in order.  A list of scattered ids runs on
+ * the SM copy kernel (K and V in one launch per 4000 pairs, the pairs passed
+ * in the kernel parameters, so the host lists may be freed on return and
+ * nothing is allocated); a list of long runs of consecutive ids (16 or more
+ * per run on average), a list whose destinations repeat or feed another
+ * pair, or a CPU pool the device cannot address (pageable memory) runs on the
+ * copy engines instead, one cudaMemcpyAsync per run.  CPU pools should be
+ * pinned: pageable ones make the copies synchronous. */
 CF_API cf_status cf_execute_block_ops(void* gpu_key_cache, void* gpu_value_cache,
                                       void* cpu_key_cache, void* cpu_value_cache,
                                       int64_t block_size_bytes, int64_t num_gpu_blocks,
@@ -372,6 +381,17 @@ CF_API cf_status cf_check_compaction_plan(const int32_t* src_ids, const int32_t*
 /* Reads (and optionally clears) the OR of all device error bits recorded by
  * kernels on `device` since the last clear.  Synchronises that device. */
 CF_API cf_status cf_get_device_errors(int32_t device, uint32_t* flags, int32_t clear);
+
+/* TEST HOOK, not for production use.  Every decode-attention launch after
+ * this call (cf_paged_attention_* of every form, process-wide) gives up a
+ * pipeline wait after wait_limit_ns nanoseconds instead of 2 s (0 restores
+ * 2 s), and with unarm_first_stage = 1 leaves the first shared-memory stage
+ * of every warp unarmed: no copy is issued for it and nothing arrives on its
+ * barrier, so that wait can only run out.  The kernel then records
+ * CF_DEVERR_TIMEOUT, writes no output and returns: the path a copy that never
+ * completes would take, exercised with no copy in flight.  (0, 0) restores
+ * normal operation.  No counterpart in CacheFlow. */
+CF_API cf_status cf_testing_set_pipeline_faults(int64_t wait_limit_ns, int32_t unarm_first_stage);
 
 /* The last cudaError_t seen by any entry point on this thread. */
 CF_API int32_t cf_last_cuda_error(void);

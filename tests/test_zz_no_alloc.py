@@ -32,9 +32,10 @@ def _call_pair(cflib, dtype, H, Hkv, D, ctx, seed):
     S = len(ctx)
     pool = sum((c + 15) // 16 for c in ctx) + 5
     tables = random_tables(rng, ctx, pool)
-    q = to_dev(host_values((S, H, D), dtype, 0.5, rng), dtype)
-    k = to_dev(host_values((pool, Hkv, 16, D), dtype, 0.5, rng), dtype)
-    v = to_dev(host_values((pool, Hkv, 16, D), dtype, 0.5, rng), dtype)
+    q_h = host_values((S, H, D), dtype, 0.5, rng)
+    k_h = host_values((pool, Hkv, 16, D), dtype, 0.5, rng)
+    v_h = host_values((pool, Hkv, 16, D), dtype, 0.5, rng)
+    q, k, v = to_dev(q_h, dtype), to_dev(k_h, dtype), to_dev(v_h, dtype)
     bt, cl = to_dev(tables), to_dev(np.array(ctx, np.int32))
     out_static = torch.full((S, H, D), 9.0, dtype=torch_dtype(dtype), device="cuda")
     out_ref = torch.empty_like(out_static)
@@ -55,7 +56,14 @@ def _call_pair(cflib, dtype, H, Hkv, D, ctx, seed):
     assert cflib.cf_paged_attention_v2_static_scratch(ctypes.byref(p), stream) == _lib.CF_OK
     torch.cuda.synchronize()
     assert ops.device_errors(0) == 0
-    assert_close(as_f64(out_static), as_f64(out_ref), dtype, "static-scratch v2 vs v2")
+    # the same kernels on the same inputs: bit-identical, not just close
+    assert torch.equal(out_static, out_ref), "static-scratch v2 differs from v2 with caller scratch"
+    # and both within the attention tolerance of the oracle
+    from oracle import oracle
+
+    code = oracle.BF16 if dtype == "bf16" else None  # f16 arrays carry their own dtype
+    want = oracle.paged_attention(q_h, k_h, v_h, tables, np.array(ctx, np.int32), scale, dtype_code=code)
+    assert_close(as_f64(out_static), want, dtype, "static-scratch v2 vs oracle")
 
 
 def test_static_scratch_matches_v2_on_two_calls_in_a_row(cflib):
@@ -76,3 +84,9 @@ def test_static_scratch_rejects_calls_that_do_not_fit(cflib):
     # 64 * 64 * 64 partitions * 130 floats = 136 MB > 16 MiB: refused, nothing launched
     assert cflib.cf_paged_attention_v2_static_scratch(ctypes.byref(p), None) == _lib.CF_ERR_WORKSPACE
     assert cflib.cf_paged_attention_v2_static_scratch(None, None) == _lib.CF_ERR_INVALID_ARGUMENT
+    # shapes the kernels do not take are refused as unsupported before any
+    # size arithmetic, however large
+    p.head_dim = 96
+    assert cflib.cf_paged_attention_v2_static_scratch(ctypes.byref(p), None) == _lib.CF_ERR_UNSUPPORTED
+    p.head_dim, p.num_seqs, p.num_heads = 128, 1 << 30, 1 << 30
+    assert cflib.cf_paged_attention_v2_static_scratch(ctypes.byref(p), None) == _lib.CF_ERR_UNSUPPORTED
