@@ -123,13 +123,33 @@ struct PairIds {
 constexpr int kCopyThreads = 256;
 constexpr int kCopyUnroll = 4;  // 16-byte vectors per thread per stream
 
-template <typename V, typename IdT, bool kSkipSame>
+// A list of up to kParamPairs (src id, dst id) pairs passed by value in the
+// kernel's parameters (CUDA 12.1+ allows 32,764 bytes of parameters on
+// sm_70 and later): the host's list needs no device copy, no staging buffer
+// and no allocation, and may be freed as soon as the launch returns.
+constexpr int kParamPairs = 4000;
+struct ParamPairs {
+  int32_t id[2 * kParamPairs];  // pair i: id[2i] = src, id[2i + 1] = dst
+};
+
+template <typename IdT>
+__device__ __forceinline__ int64_t pair_src(const PairIds<IdT>& ids, int64_t i) {
+  return (int64_t)ids.src[i * ids.stride];
+}
+template <typename IdT>
+__device__ __forceinline__ int64_t pair_dst(const PairIds<IdT>& ids, int64_t i) {
+  return (int64_t)ids.dst[i * ids.stride];
+}
+__device__ __forceinline__ int64_t pair_src(const ParamPairs& ids, int64_t i) { return ids.id[2 * i]; }
+__device__ __forceinline__ int64_t pair_dst(const ParamPairs& ids, int64_t i) { return ids.id[2 * i + 1]; }
+
+template <typename V, typename Ids, bool kSkipSame>
 __global__ void __launch_bounds__(kCopyThreads)
-    pair_copy_kernel(PairStreams st, PairIds<IdT> ids, int32_t num_pairs, int64_t vecs_per_block,
+    pair_copy_kernel(PairStreams st, Ids ids, int32_t num_pairs, int64_t vecs_per_block,
                      int64_t num_src_blocks, int64_t num_dst_blocks) {
   for (int64_t pair = blockIdx.y; pair < num_pairs; pair += gridDim.y) {
-    const int64_t s = (int64_t)ids.src[pair * ids.stride];
-    const int64_t d = (int64_t)ids.dst[pair * ids.stride];
+    const int64_t s = pair_src(ids, pair);
+    const int64_t d = pair_dst(ids, pair);
     if (s < 0 || s >= num_src_blocks || d < 0 || d >= num_dst_blocks) {
       if (blockIdx.x == 0 && threadIdx.x == 0) cache_error(CF_DEVERR_BLOCK_ID);
       continue;
@@ -196,8 +216,8 @@ int vector_bytes(std::initializer_list<const void*> ptrs, int64_t bytes) {
   return w < 4 ? 1 : w;
 }
 
-template <typename IdT, bool kSkipSame>
-cf_status launch_pairs(const PairStreams& st, const PairIds<IdT>& ids, int32_t num_pairs,
+template <typename Ids, bool kSkipSame>
+cf_status launch_pairs(const PairStreams& st, const Ids& ids, int32_t num_pairs,
                        int64_t block_bytes, int64_t num_src, int64_t num_dst,
                        cudaStream_t stream) {
   if (num_pairs == 0) return CF_OK;
@@ -210,13 +230,13 @@ cf_status launch_pairs(const PairStreams& st, const PairIds<IdT>& ids, int32_t n
   if (chunks > 0x7fffffff) return CF_ERR_UNSUPPORTED;
   dim3 grid((unsigned)chunks, (unsigned)(num_pairs < 65535 ? num_pairs : 65535));
   if (w == 16)
-    pair_copy_kernel<uint4, IdT, kSkipSame>
+    pair_copy_kernel<uint4, Ids, kSkipSame>
         <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
   else if (w == 4)
-    pair_copy_kernel<uint32_t, IdT, kSkipSame>
+    pair_copy_kernel<uint32_t, Ids, kSkipSame>
         <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
   else
-    pair_copy_kernel<uint8_t, IdT, kSkipSame>
+    pair_copy_kernel<uint8_t, Ids, kSkipSame>
         <<<grid, kCopyThreads, 0, stream>>>(st, ids, num_pairs, vecs, num_src, num_dst);
   return check_launch();
 }
@@ -259,7 +279,7 @@ cf_status launch_copy_pairs64(void* key_cache, void* value_cache, const int64_t*
                  {(uint8_t*)key_cache, (uint8_t*)value_cache},
                  2};
   PairIds<int64_t> ids{mapping, mapping + 1, 2};
-  return launch_pairs<int64_t, false>(st, ids, num_pairs, block_bytes, num_blocks, num_blocks,
+  return launch_pairs<PairIds<int64_t>, false>(st, ids, num_pairs, block_bytes, num_blocks, num_blocks,
                                       stream);
 }
 
@@ -269,7 +289,7 @@ cf_status launch_swap_pairs64(const void* src_cache, void* dst_cache, const int6
   PairIds<int64_t> ids{mapping, mapping + 1, 2};
   // Pool sizes are unknown to the reference interface: ids are checked >= 0 only.
   const int64_t unchecked = INT64_MAX / (block_bytes > 0 ? block_bytes : 1);
-  return launch_pairs<int64_t, false>(st, ids, num_pairs, block_bytes, unchecked, unchecked,
+  return launch_pairs<PairIds<int64_t>, false>(st, ids, num_pairs, block_bytes, unchecked, unchecked,
                                       stream);
 }
 
@@ -280,8 +300,28 @@ cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t
                  {(uint8_t*)key_cache, (uint8_t*)value_cache},
                  2};
   PairIds<int32_t> ids{src_ids, dst_ids, 1};
-  return launch_pairs<int32_t, true>(st, ids, num_moves, block_bytes, num_blocks, num_blocks,
+  return launch_pairs<PairIds<int32_t>, true>(st, ids, num_moves, block_bytes, num_blocks, num_blocks,
                                      stream);
+}
+
+cf_status launch_host_pairs(const void* src_k, void* dst_k, const void* src_v, void* dst_v,
+                            const int64_t* host_pairs, int32_t num_pairs, int64_t block_bytes,
+                            int64_t num_src_blocks, int64_t num_dst_blocks, cudaStream_t stream) {
+  PairStreams st{{(const uint8_t*)src_k, (const uint8_t*)src_v}, {(uint8_t*)dst_k, (uint8_t*)dst_v}, 2};
+  ParamPairs pl;
+  for (int32_t first = 0; first < num_pairs; first += kParamPairs) {
+    const int32_t n = num_pairs - first < kParamPairs ? num_pairs - first : kParamPairs;
+    for (int32_t i = 0; i < n; ++i) {
+      const int64_t s = host_pairs[2 * (int64_t)(first + i)], d = host_pairs[2 * (int64_t)(first + i) + 1];
+      if (s < 0 || s > INT32_MAX || d < 0 || d > INT32_MAX) return CF_ERR_INVALID_ARGUMENT;
+      pl.id[2 * i] = (int32_t)s;
+      pl.id[2 * i + 1] = (int32_t)d;
+    }
+    const cf_status r = launch_pairs<ParamPairs, false>(st, pl, n, block_bytes, num_src_blocks,
+                                                        num_dst_blocks, stream);
+    if (r != CF_OK) return r;
+  }
+  return CF_OK;
 }
 
 cf_status launch_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,

@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <unordered_set>
 #include <vector>
 
 #include "../../include/cacheflow_b200.h"
@@ -425,11 +426,16 @@ cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
       return CF_ERR_INVALID_ARGUMENT;
   const uint8_t* src = static_cast<const uint8_t*>(src_cache);
   uint8_t* dst = static_cast<uint8_t*>(dst_cache);
+  // Within one pool a merged run must not read a block it also writes: the
+  // pairs apply in order, so (1->2, 2->3) copies block 1 into both, which one
+  // overlapping copy of blocks 1..2 onto 2..3 would not do.
+  const bool same_pool = src_cache == dst_cache;
   int32_t i = 0;
   while (i < num_pairs) {
     const int64_t s0 = host_block_mapping[2 * i], d0 = host_block_mapping[2 * i + 1];
+    const int64_t max_run = same_pool ? (s0 == d0 ? 1 : (s0 < d0 ? d0 - s0 : s0 - d0)) : INT64_MAX;
     int32_t run = 1;
-    while (i + run < num_pairs && host_block_mapping[2 * (i + run)] == s0 + run &&
+    while (i + run < num_pairs && run < max_run && host_block_mapping[2 * (i + run)] == s0 + run &&
            host_block_mapping[2 * (i + run) + 1] == d0 + run)
       ++run;
     cudaError_t e = cudaMemcpyAsync(dst + d0 * block_size_bytes, src + s0 * block_size_bytes,
@@ -466,21 +472,72 @@ cf_status cf_execute_block_ops(void* gpu_key_cache, void* gpu_value_cache, void*
     return CF_ERR_INVALID_ARGUMENT;
   if ((num_swaps_out + num_swaps_in) > 0 && (!cpu_key_cache || !cpu_value_cache))
     return CF_ERR_INVALID_ARGUMENT;
-  // Swap-outs free GPU blocks that swap-ins and copies may then reuse.
+  // Swap-outs free GPU blocks that swap-ins and copies may then reuse: the
+  // three lists run in that order on the stream.  Each list goes either to
+  // the SM copy kernel (both caches in one launch per 4000 pairs, the list
+  // passed in the kernel parameters) or to the copy engines (one
+  // cudaMemcpyAsync per contiguous run):
+  //  * copy engines when the list is made of long runs (at least
+  //    kDmaMinRun consecutive ids per run on average), where one DMA moves
+  //    many blocks at the host link's full rate;
+  //  * copy engines when a CPU pool is not addressable from the device
+  //    (pageable memory), since the kernel cannot read it;
+  //  * copy engines when a pair's destination is another pair's source or
+  //    destination in the same list: the kernel runs the pairs of a launch
+  //    concurrently, the copy engines apply them in order.
+  //  Otherwise (scattered ids, the scheduler's usual lists,
+  //  scheduler.cpp:220-224,249-254) the SM kernel, which keeps many blocks in
+  //  flight at once.
+  constexpr int64_t kDmaMinRun = 16;
+  const bool cpu_mapped = (num_swaps_out + num_swaps_in) == 0 ||
+                          (device_view(cpu_key_cache) != nullptr && device_view(cpu_value_cache) != nullptr);
+  auto use_kernel = [&](const int64_t* pairs, int32_t n, bool crosses_host) {
+    if (crosses_host && !cpu_mapped) return false;
+    int64_t runs = 0;
+    for (int32_t i = 0; i < n; ++i)
+      if (i == 0 || pairs[2 * i] != pairs[2 * i - 2] + 1 || pairs[2 * i + 1] != pairs[2 * i - 1] + 1) ++runs;
+    if ((int64_t)n >= kDmaMinRun * runs) return false;
+    std::unordered_set<int64_t> dsts;
+    dsts.reserve((size_t)n * 2);
+    for (int32_t i = 0; i < n; ++i) {
+      if (pairs[2 * i] > INT32_MAX || pairs[2 * i + 1] > INT32_MAX) return false;
+      if (!dsts.insert(pairs[2 * i + 1]).second) return false;  // written twice
+    }
+    if (!crosses_host)
+      for (int32_t i = 0; i < n; ++i)
+        if (dsts.count(pairs[2 * i])) return false;  // read after another pair writes it
+    return true;
+  };
   const struct {
-    void* src;
-    void* dst;
+    void* src_k;
+    void* src_v;
+    void* dst_k;
+    void* dst_v;
     const int64_t* pairs;
     int32_t n;
-  } steps[6] = {{gpu_key_cache, cpu_key_cache, swaps_out, num_swaps_out},
-                {gpu_value_cache, cpu_value_cache, swaps_out, num_swaps_out},
-                {cpu_key_cache, gpu_key_cache, swaps_in, num_swaps_in},
-                {cpu_value_cache, gpu_value_cache, swaps_in, num_swaps_in},
-                {gpu_key_cache, gpu_key_cache, copies, num_copies},
-                {gpu_value_cache, gpu_value_cache, copies, num_copies}};
+    int64_t num_src, num_dst;
+    bool crosses_host;
+  } steps[3] = {
+      {gpu_key_cache, gpu_value_cache, cpu_key_cache, cpu_value_cache, swaps_out, num_swaps_out,
+       num_gpu_blocks, num_cpu_blocks, true},
+      {cpu_key_cache, cpu_value_cache, gpu_key_cache, gpu_value_cache, swaps_in, num_swaps_in,
+       num_cpu_blocks, num_gpu_blocks, true},
+      {gpu_key_cache, gpu_value_cache, gpu_key_cache, gpu_value_cache, copies, num_copies,
+       num_gpu_blocks, num_gpu_blocks, false}};
   for (const auto& st : steps) {
     if (st.n == 0) continue;
-    const cf_status r = cf_swap_blocks_dma(st.src, st.dst, st.pairs, st.n, block_size_bytes, stream);
+    cf_status r;
+    if (use_kernel(st.pairs, st.n, st.crosses_host)) {
+      const void* sk = st.crosses_host ? device_view(st.src_k) : st.src_k;
+      const void* sv = st.crosses_host ? device_view(st.src_v) : st.src_v;
+      void* dk = const_cast<void*>(st.crosses_host ? device_view(st.dst_k) : st.dst_k);
+      void* dv = const_cast<void*>(st.crosses_host ? device_view(st.dst_v) : st.dst_v);
+      r = launch_host_pairs(sk, dk, sv, dv, st.pairs, st.n, block_size_bytes, st.num_src, st.num_dst,
+                            (cudaStream_t)stream);
+    } else {
+      r = cf_swap_blocks_dma(st.src_k, st.dst_k, st.pairs, st.n, block_size_bytes, stream);
+      if (r == CF_OK) r = cf_swap_blocks_dma(st.src_v, st.dst_v, st.pairs, st.n, block_size_bytes, stream);
+    }
     if (r != CF_OK) return r;
   }
   return CF_OK;

@@ -71,6 +71,12 @@ cf_status launch_swap_pairs64(const void* src_cache, void* dst_cache, const int6
 cf_status launch_move_blocks32(void* key_cache, void* value_cache, const int32_t* src_ids,
                                const int32_t* dst_ids, int32_t num_moves, int64_t block_bytes,
                                int64_t num_blocks, cudaStream_t stream);
+// K and V blocks copied for a HOST list of int64 (src, dst) pairs (ids below
+// 2^31), the list passed by value in the kernel parameters (no device copy of
+// it); one launch per 4000 pairs.  Pairs of one launch run concurrently.
+cf_status launch_host_pairs(const void* src_k, void* dst_k, const void* src_v, void* dst_v,
+                            const int64_t* host_pairs, int32_t num_pairs, int64_t block_bytes,
+                            int64_t num_src_blocks, int64_t num_dst_blocks, cudaStream_t stream);
 cf_status launch_memset_blocks(void* cache, const int32_t* ids, int32_t num_listed,
                                int64_t block_bytes, int64_t num_blocks, cudaStream_t stream);
 cf_status launch_build_decode_inputs(const int32_t* positions, const int64_t* block_offsets,

@@ -474,8 +474,9 @@ def execute_block_ops(gpu_key_cache, gpu_value_cache, cpu_key_cache, cpu_value_c
                       swaps_in=None, copies=None) -> None:
     """One scheduling step's block operations (SchedulerOutput::block_swaps_out,
     block_swaps_in, block_copies): swap-outs, swap-ins, then copy-on-write
-    copies, for K and V, on the copy engines.  Pair lists are host int64
-    arrays [n, 2] of (src, dst) block ids."""
+    copies, for K and V.  Pair lists are host int64 arrays [n, 2] of (src, dst)
+    block ids; scattered lists run on the SM copy kernel, lists of long
+    contiguous runs (and pageable CPU pools) on the copy engines."""
     lib = _lib.load()
 
     def host_pairs(x):

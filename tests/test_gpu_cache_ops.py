@@ -278,3 +278,65 @@ def test_execute_block_ops_matches_sequential_application(cflib):
     assert torch.equal(ck, want[2]) and torch.equal(cv, want[3])
     with pytest.raises(ops.CacheFlowError):  # a CPU id past the pool: nothing is enqueued
         ops.execute_block_ops(dk, dv, ck, cv, swaps_out=np.array([[0, ncpu]], np.int64))
+
+
+def _apply_host(want, swaps_out, swaps_in, copies):
+    for src, dst in swaps_out:
+        want[2][dst] = want[0][src]
+        want[3][dst] = want[1][src]
+    for src, dst in swaps_in:
+        want[0][dst] = want[2][src]
+        want[1][dst] = want[3][src]
+    for src, dst in copies:
+        want[0][dst] = want[0][src]
+        want[1][dst] = want[1][src]
+
+
+@pytest.mark.parametrize("case", ["many_scattered", "long_runs", "chained_copies", "pageable_cpu_pool"])
+def test_execute_block_ops_kernel_and_copy_engine_paths(cflib, case):
+    """Every route of cf_execute_block_ops gives the sequential result:
+    more than one kernel launch's worth of scattered pairs (4000 per launch),
+    lists of long consecutive runs (copy engines), COW copies that form a
+    chain (a destination read by a later pair: copy engines, in order), and a
+    pageable CPU pool the kernel cannot address (copy engines)."""
+    import torch
+
+    from cacheflow_b200 import ops
+
+    rng = np.random.default_rng({"many_scattered": 41, "long_runs": 42, "chained_copies": 43,
+                                 "pageable_cpu_pool": 44}[case])
+    ngpu, ncpu, shape = 12000, 9000, (2, 16, 8)  # 512-byte bf16 blocks
+    if case != "many_scattered":
+        ngpu, ncpu = 600, 400
+    gk = torch.from_numpy(rng.standard_normal((ngpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    gv = torch.from_numpy(rng.standard_normal((ngpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    ck = torch.from_numpy(rng.standard_normal((ncpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    cv = torch.from_numpy(rng.standard_normal((ncpu,) + shape).astype(np.float32)).to(torch.bfloat16)
+    if case != "pageable_cpu_pool":
+        ck, cv = ck.pin_memory(), cv.pin_memory()
+    if case == "many_scattered":
+        g = rng.permutation(ngpu)
+        swaps_out = np.stack([g[:8500], rng.permutation(ncpu)[:8500]], 1)
+        swaps_in = np.stack([rng.permutation(ncpu)[:4100], g[:4100]], 1)  # reuse swapped-out GPU blocks
+        copies = np.stack([g[8500:8600], g[8600:8700]], 1)
+    elif case == "long_runs":
+        swaps_out = np.stack([np.arange(100, 300), np.arange(50, 250)], 1)
+        swaps_in = np.stack([np.arange(0, 64), np.arange(100, 164)], 1)
+        copies = np.stack([np.arange(400, 480), np.arange(500, 580)], 1)
+    elif case == "chained_copies":
+        swaps_out = np.stack([rng.permutation(ngpu)[:20], rng.permutation(ncpu)[:20]], 1)
+        swaps_in = np.zeros((0, 2), np.int64)
+        copies = np.array([[1, 2], [2, 3], [3, 4], [9, 7], [7, 11]], np.int64)  # 2..4 all become block 1
+    else:
+        swaps_out = np.stack([rng.permutation(ngpu)[:50], rng.permutation(ncpu)[:50]], 1)
+        swaps_in = np.stack([rng.permutation(ncpu)[:30], rng.permutation(ngpu)[:30]], 1)
+        copies = np.zeros((0, 2), np.int64)
+    swaps_out, swaps_in, copies = (np.ascontiguousarray(x, np.int64) for x in (swaps_out, swaps_in, copies))
+    want = [t.clone() for t in (gk, gv, ck, cv)]
+    _apply_host(want, swaps_out, swaps_in, copies)
+    dk, dv = gk.cuda(), gv.cuda()
+    ops.execute_block_ops(dk, dv, ck, cv, swaps_out, swaps_in, copies)
+    torch.cuda.synchronize()
+    assert ops.device_errors(0) == 0
+    assert torch.equal(dk.cpu(), want[0]) and torch.equal(dv.cpu(), want[1])
+    assert torch.equal(ck, want[2]) and torch.equal(cv, want[3])
