@@ -162,6 +162,7 @@ SIGNATURES = {
     "cf_last_cuda_error": (c_int32, []),
     "cf_status_string": (c_char_p, [c_int32]),
     "cf_abi_version": (c_int32, []),
+    "cf_testing_set_pipeline_faults": (c_int32, [c_int64, c_int32]),
 }
 
 # The C++ entry points with CacheFlow's signatures (mangled names).

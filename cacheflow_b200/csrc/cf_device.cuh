@@ -199,15 +199,17 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // CF_DEVERR_TIMEOUT and returns instead of spinning forever.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Waits for phase `parity` of barrier `bar` to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Waits for phase `parity` of barrier `bar` to complete; false once
+// `limit_ns` of %globaltimer have passed without it.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

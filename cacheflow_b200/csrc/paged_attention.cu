@@ -36,6 +36,7 @@
 //     otherwise the partition writes (max logit, exp-sum, normalised partial
 //     output) and the reduce kernel merges partitions with the log-sum-exp
 //     weights  w_p = exp_sum_p * exp(max_p - max).
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -85,6 +86,12 @@ struct AttnArgs {
   void* v_cache_w;
   float v_scale;                // fp8 caches: V = stored * v_scale (else 1)
   float k_scale;                // fp8 caches: K = stored * k_scale (appends store K / k_scale)
+  // Pipeline waits give up after this long (kWaitLimitNs unless a test
+  // shortened it with cf_testing_set_pipeline_faults).
+  uint64_t wait_limit_ns;
+  // Test hook: nonzero leaves the first stage of every warp unarmed (no copy
+  // issued, no arrive), so its wait can only run out.
+  int32_t unarm_first_stage;
 };
 
 // ---------------------------------------------------------------------------
@@ -813,6 +820,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     return j < nb ? table[(warp + j * NW) / kSubs] : 0;
   };
   auto issue = [&](int j, int phys) {  // lane 0 only
+    if (a.unarm_first_stage && j == 0) return;  // test hook: the stage never completes
     const int s = j % S;
     const uint32_t bar = smem_addr(&bars[s]);
     const int u = warp + j * NW;
@@ -868,7 +876,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   for (int i = 0; i < nmain; ++i) {
     const int s = i % S;
     const uint32_t parity = (uint32_t)(i / S) & 1u;
-    const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), parity);
+    const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), parity, a.wait_limit_ns);
     if (!__all_sync(0xffffffffu, ready)) {
       // A copy never completed: record it, wait (bounded) for every copy this
       // warp still has in flight so none lands after the CTA exits, and stop.
@@ -876,7 +884,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
         attn_error(CF_DEVERR_TIMEOUT);
         const int last = (i + S < nb ? i + S : nb);
         for (int k = i; k < last; ++k)
-          mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u);
+          mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u, a.wait_limit_ns);
       }
       __syncwarp();
       ok = false;
@@ -902,11 +910,11 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     const int i = nb - 1;
     if (ok && i >= 0) {
       const int s = i % S;
-      const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u);
+      const bool ready = mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u, a.wait_limit_ns);
       if (!__all_sync(0xffffffffu, ready)) {
         if (lane == 0) {  // as in the loop: wait (bounded) once more for the copy in flight
           attn_error(CF_DEVERR_TIMEOUT);
-          mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u);
+          mbar_wait_bounded(smem_addr(&bars[s]), (uint32_t)(i / S) & 1u, a.wait_limit_ns);
         }
         ok = false;
       } else {
@@ -937,7 +945,12 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
   float* ml = mm + NW * HG;
   cons.store(mo + warp * HG * D, mm + warp * HG, ml + warp * HG, lane);
   const int all_ok = __syncthreads_and(ok ? 1 : 0);
-  if (!all_ok) return;
+  if (!all_ok) {
+    // a wait ran out: no output; the append's staging copies (cp.async, if
+    // this thread issued any) land before the CTA leaves
+    if constexpr (kAppend) cp_async_wait_all();
+    return;
+  }
 
   const size_t H = (size_t)a.num_heads;
   for (int idx = threadIdx.x; idx < nheads * D; idx += NW * 32) {
@@ -1262,6 +1275,10 @@ bool attention_fp8_supported(int32_t head_dim, int32_t block_size, int32_t dtype
          (head_dim == 128 || head_dim == 256);
 }
 
+// Test hooks (cf_testing_set_pipeline_faults), read at every launch.
+std::atomic<int64_t> g_test_wait_limit_ns{0};
+std::atomic<int32_t> g_test_unarm_first_stage{0};
+
 cf_status launch_paged_attention(const AttnLaunch& l) {
   const cf_paged_attention_params& p = *l.p;
   if (p.num_seqs == 0) return CF_OK;
@@ -1289,6 +1306,11 @@ cf_status launch_paged_attention(const AttnLaunch& l) {
   a.slot_mapping = l.slot_mapping;
   a.k_cache_w = const_cast<void*>(p.key_cache);
   a.v_cache_w = const_cast<void*>(p.value_cache);
+  {
+    const int64_t lim = g_test_wait_limit_ns.load(std::memory_order_relaxed);
+    a.wait_limit_ns = lim > 0 ? (uint64_t)lim : kWaitLimitNs;
+    a.unarm_first_stage = g_test_unarm_first_stage.load(std::memory_order_relaxed);
+  }
   int grid_x = 1;
   if (l.part_tokens > 0 && l.part_max != nullptr) {
     a.part_blocks = l.part_tokens / kBlockTokens;
@@ -1324,3 +1346,11 @@ cf_status attention_read_errors(uint32_t* bits, bool clear) {
 }
 
 }  // namespace cfb
+
+// Test hook of the decode kernels' bounded waits (declared in the C ABI).
+extern "C" cf_status cf_testing_set_pipeline_faults(int64_t wait_limit_ns, int32_t unarm_first_stage) {
+  if (wait_limit_ns < 0 || unarm_first_stage < 0 || unarm_first_stage > 1) return CF_ERR_INVALID_ARGUMENT;
+  cfb::g_test_wait_limit_ns.store(wait_limit_ns, std::memory_order_relaxed);
+  cfb::g_test_unarm_first_stage.store(unarm_first_stage, std::memory_order_relaxed);
+  return CF_OK;
+}
