@@ -2,7 +2,7 @@
  * cacheflow_b200.h -- C ABI of the B200 (sm_100a) KV-cache kernel layer.
  *
  * Every entry point is a drop-in for one operator of CacheFlow's CUDA layer
- * (src/cacheflow/cuda/*.cuh in the CacheFlow sources); the comment above each
+ * (the headers under src/cacheflow/cuda/ in the CacheFlow sources); the comment above each
  * declaration names the reference interface it replaces (file:line).
  *
  * Conventions shared by all entry points:
@@ -310,10 +310,11 @@ CF_API cf_status cf_swap_blocks(const void* src_cache, void* dst_cache,
                          const int64_t* block_mapping, int32_t num_pairs,
                          int64_t block_size_bytes, void* stream);
 
-/* Same copy as cf_swap_blocks, with block_mapping in HOST memory: pairs whose
- * source and destination ids both advance by one are merged into one
- * cudaMemcpyAsync, so the copy engines move them (no SM time).  Use a side
- * stream so the swap overlaps attention. */
+/* Same copy as cf_swap_blocks, with block_mapping in HOST memory, the pairs
+ * applied in order: pairs whose source and destination ids both advance by
+ * one are merged into one cudaMemcpyAsync (within one pool only while the
+ * merged run reads no block it writes), so the copy engines move them (no SM
+ * time).  Use a side stream so the swap overlaps attention. */
 CF_API cf_status cf_swap_blocks_dma(const void* src_cache, void* dst_cache,
                              const int64_t* host_block_mapping,
                              int32_t num_pairs, int64_t block_size_bytes,

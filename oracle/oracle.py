@@ -25,13 +25,27 @@ DTYPE_CODE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1}
 BF16 = 2  # numpy has no bfloat16: bf16 arrays are carried as uint16 bit patterns
 
 
+REF_API_LIB = HERE / "_ref" / "libcf_ref_api.so"
+REF_ENGINE_LIB = HERE / "_ref" / "libcf_ref_engine.so"
+
+
+def reference_dir() -> Path | None:
+    """The CacheFlow checkout: $CF_REFERENCE_DIR, else a `reference` directory
+    beside this checkout; None when neither holds src/cacheflow."""
+    env = os.environ.get("CF_REFERENCE_DIR")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "src" / "cacheflow").is_dir() else None
+
+
 def build(with_reference: bool | None = None) -> None:
     """Builds the oracle (and, when the reference checkout exists, oracle/_ref)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "libcf_oracle.so"], check=True)
-    ref = os.environ.get("CF_REFERENCE_DIR", "/root/reference")
+    ref = reference_dir()
     if with_reference is None:
-        with_reference = Path(ref, "src", "cacheflow").is_dir()
+        with_reference = ref is not None
     if with_reference:
+        if ref is None:
+            raise RuntimeError("CacheFlow sources not found: set CF_REFERENCE_DIR")
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
 
 
@@ -255,6 +269,104 @@ class RefCuda:
         L.ref_compact_kv_cache.argtypes = [c_void_p] * 4 + [c_int32] * 4
         L.ref_memset_blocks.argtypes = [c_void_p] * 2 + [c_int32] * 2
         self.lib = L
+
+
+class RefApi:
+    """CacheFlow's cacheflow::cuda::launch_* call shape, compiled against its
+    unchanged headers and linked to libcacheflow_b200.so (ref_api_driver.cpp):
+    the reference-facing C++ entry points of the product, run on the GPU."""
+
+    def __init__(self):
+        if not REF_API_LIB.exists():
+            raise FileNotFoundError(f"{REF_API_LIB} not built (make -C oracle ref)")
+        L = ctypes.CDLL(str(REF_API_LIB), mode=os.RTLD_LOCAL)
+        L.api_paged_attention_v1.argtypes = [c_void_p] * 6 + [c_float] + [c_int32] * 7 + [c_void_p]
+        L.api_paged_attention_v2.argtypes = ([c_void_p] * 6 + [c_float] + [c_int32] * 7 + [c_void_p] * 3
+                                             + [c_int32, c_void_p])
+        L.api_reshape_and_cache.argtypes = [c_void_p] * 5 + [c_int32] * 4 + [c_void_p]
+        L.api_copy_blocks.argtypes = [c_void_p] * 3 + [c_int32] * 4 + [c_void_p]
+        L.api_swap_blocks.argtypes = [c_void_p] * 3 + [c_int32] * 2 + [c_void_p]
+        L.api_compact_kv_cache.argtypes = [c_void_p] * 4 + [c_int32] * 4 + [c_void_p]
+        L.api_memset_blocks.argtypes = [c_void_p] * 2 + [c_int32] * 2 + [c_void_p]
+        L.api_async_memcpy_d2d.argtypes = [c_void_p, c_void_p, ctypes.c_size_t, c_void_p]
+        L.api_synchronize_device.restype = None
+        self.lib = L
+
+
+class RefEngine:
+    """CacheFlow's Scheduler / BatchManager / BlockManager (reference sources)
+    over the C++ decode step of include/cacheflow_b200_engine.hpp
+    (ref_engine_driver.cpp)."""
+
+    COUNTS = ("rows", "swaps_out", "swaps_in", "copies", "seqs", "decode_rows", "chunks", "fused")
+
+    def __init__(self, num_heads, num_kv_heads, head_dim, dtype_code, num_gpu_blocks, num_cpu_blocks, max_num_seqs,
+                 max_batched_tokens, max_rows, max_blocks_per_seq, gpu_k, gpu_v, cpu_k, cpu_v):
+        if not REF_ENGINE_LIB.exists():
+            raise FileNotFoundError(f"{REF_ENGINE_LIB} not built (make -C oracle ref)")
+        L = ctypes.CDLL(str(REF_ENGINE_LIB), mode=os.RTLD_LOCAL)
+        L.eng_create.restype = c_void_p
+        L.eng_create.argtypes = [c_int32] * 4 + [c_int64] * 2 + [c_int32] * 4 + [c_void_p] * 4 + [POINTER(c_int32)]
+        L.eng_destroy.argtypes = [c_void_p]
+        L.eng_add_request.argtypes = [c_void_p, ctypes.c_uint64, c_int32, c_int32]
+        L.eng_has_pending.restype = c_int32
+        L.eng_has_pending.argtypes = [c_void_p]
+        L.eng_schedule.restype = c_int32
+        L.eng_schedule.argtypes = [c_void_p, c_void_p, c_void_p]
+        L.eng_rows.restype = c_int32
+        L.eng_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32]
+        L.eng_block_ops.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p]
+        L.eng_attend.restype = c_int32
+        L.eng_attend.argtypes = [c_void_p] * 6
+        L.eng_finish_step.argtypes = [c_void_p, c_void_p, c_int32]
+        self.lib = L
+        st = c_int32(-1)
+        self.h = L.eng_create(num_heads, num_kv_heads, head_dim, dtype_code, num_gpu_blocks, num_cpu_blocks,
+                              max_num_seqs, max_batched_tokens, max_rows, max_blocks_per_seq, gpu_k, gpu_v, cpu_k,
+                              cpu_v, ctypes.byref(st))
+        if not self.h:
+            raise RuntimeError(f"eng_create failed: status {st.value}")
+        self.max_blocks = max_blocks_per_seq
+
+    def add_request(self, rid: int, prompt_len: int, max_tokens: int) -> None:
+        self.lib.eng_add_request(self.h, rid, prompt_len, max_tokens)
+
+    def has_pending(self) -> bool:
+        return bool(self.lib.eng_has_pending(self.h))
+
+    def schedule(self, stream) -> dict:
+        c = np.zeros(8, np.int32)
+        st = self.lib.eng_schedule(self.h, stream, _p(c))
+        if st != 0:
+            raise RuntimeError(f"eng_schedule: status {st}")
+        return dict(zip(self.COUNTS, (int(x) for x in c)))
+
+    def rows(self, n: int):
+        ids = np.zeros(max(n, 1), np.uint64)
+        pos = np.zeros(max(n, 1), np.int32)
+        tab = np.full((max(n, 1), self.max_blocks), -1, np.int32)
+        if self.lib.eng_rows(self.h, _p(ids), _p(pos), _p(tab), self.max_blocks) != 0:
+            raise RuntimeError("eng_rows failed")
+        return ids[:n], pos[:n], tab[:n]
+
+    def block_ops(self, counts: dict):
+        out = np.zeros((max(counts["swaps_out"], 1), 2), np.int64)
+        inn = np.zeros((max(counts["swaps_in"], 1), 2), np.int64)
+        cp = np.zeros((max(counts["copies"], 1), 2), np.int64)
+        self.lib.eng_block_ops(self.h, _p(out), _p(inn), _p(cp))
+        return out[: counts["swaps_out"]], inn[: counts["swaps_in"]], cp[: counts["copies"]]
+
+    def attend(self, q, out, k_new, v_new, stream) -> int:
+        return self.lib.eng_attend(self.h, q, out, k_new, v_new, stream)
+
+    def finish_step(self, tokens: np.ndarray) -> None:
+        t = np.ascontiguousarray(tokens, np.int32)
+        self.lib.eng_finish_step(self.h, _p(t) if t.size else None, int(t.size))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.eng_destroy(self.h)
+            self.h = None
 
 
 class RefCpu:

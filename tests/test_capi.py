@@ -61,11 +61,16 @@ def test_compat_header_declares_reference_signatures():
         assert re.search(rf"CF_COMPAT_API\s+\w+\s+{fn}\(", text), fn
 
 
-REF = Path(os.environ.get("CF_REFERENCE_DIR", "/root/reference"))
+def _reference_dir():
+    from oracle import oracle
+
+    return oracle.reference_dir()
 
 
-@pytest.mark.skipif(not (REF / "src" / "cacheflow").is_dir() or shutil.which("g++") is None,
-                    reason="CacheFlow sources not present")
+REF = _reference_dir()
+
+
+@pytest.mark.skipif(REF is None or shutil.which("g++") is None, reason="CacheFlow sources not present")
 def test_reference_host_code_links_against_library(cflib, tmp_path):
     """CacheFlow's own decode engine, compiled with CUDA enabled against its own
     unchanged headers, links against libcacheflow_b200.so with no undefined
@@ -222,3 +227,32 @@ def test_engine_rejects_unknown_kernel_choice_before_touching_a_gpu():
 
     with pytest.raises(ValueError):
         DecodeEngine(torch.empty((4, 2, 16, 64)), torch.empty((4, 2, 16, 64)), 2, 1, 1, kernel="v3")
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="g++ not present")
+def test_engine_header_compiles_against_cacheflow_shaped_types(tmp_path):
+    """include/cacheflow_b200_engine.hpp needs only the C ABI header and the
+    CUDA runtime: it compiles warning-free against types with the fields of
+    CacheFlow's DecodeBatch and SchedulerOutput (batch_manager.h:13-36,
+    scheduler.h:16-30) without CacheFlow's headers."""
+    src = tmp_path / "use_engine.cpp"
+    src.write_text(
+        "#include \"cacheflow_b200_engine.hpp\"\n"
+        "#include <cstdint>\n#include <vector>\n"
+        "struct Entry { uint64_t seq_id; int32_t token; int32_t position; std::vector<int32_t> block_table;"
+        " bool is_prefill; };\n"
+        "struct Batch { std::vector<Entry> entries; size_t total_tokens = 0; };\n"
+        "struct BlockOp { uint64_t seq_id; int32_t src; int32_t dst; };\n"
+        "struct Output { std::vector<BlockOp> block_copies, block_swaps_in, block_swaps_out; };\n"
+        "int run(void* k, void* v, void* q, void* o, cudaStream_t s) {\n"
+        "  cacheflow_b200::StepShape sh; sh.num_heads = 32; sh.num_kv_heads = 8; sh.head_dim = 128;\n"
+        "  sh.num_gpu_blocks = 1024; sh.max_rows = 256; sh.max_blocks_per_seq = 512;\n"
+        "  cacheflow_b200::DecodeStep step(sh, k, v);\n"
+        "  Batch b; b.entries.push_back({1, 7, 20, {3, 4}, false}); Output so;\n"
+        "  if (step.execute_block_ops(so, s) != CF_OK) return 1;\n"
+        "  if (step.stage(b, s) != CF_OK) return 2;\n"
+        "  return step.attend(q, o, nullptr, nullptr, s);\n"
+        "}\n")
+    r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", f"-I{ROOT / 'include'}",
+                        "-I/usr/local/cuda/include", str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
