@@ -129,28 +129,40 @@ def plan_rebalance(loads: list[int], seq_lens: list[dict[int, int]], tolerance: 
     return moves
 
 
-def gather_blocks_cuda(cache, ids: list[int], out) -> None:
+def _pairs(src, dst, device):
+    import torch
+
+    m = np.stack([np.asarray(src, np.int64), np.asarray(dst, np.int64)], 1)
+    return torch.from_numpy(m).to(device)
+
+
+def gather_blocks_cuda(cache, ids, out) -> None:
     """out[i] = cache[ids[i]] with the library's block-copy kernel."""
-    import torch
-
     from . import ops
 
-    if not ids:
+    if len(ids) == 0:
         return
-    m = torch.tensor([[b, i] for i, b in enumerate(ids)], dtype=torch.int64).to(cache.device, non_blocking=True)
-    ops.swap_blocks(cache, out, m, stream_tensor=cache)
+    ops.swap_blocks(cache, out, _pairs(ids, np.arange(len(ids)), cache.device), stream_tensor=cache)
 
 
-def scatter_blocks_cuda(buf, cache, ids: list[int]) -> None:
+def scatter_blocks_cuda(buf, cache, ids) -> None:
     """cache[ids[i]] = buf[i] with the library's block-copy kernel."""
-    import torch
-
     from . import ops
 
-    if not ids:
+    if len(ids) == 0:
         return
-    m = torch.tensor([[i, b] for i, b in enumerate(ids)], dtype=torch.int64).to(cache.device, non_blocking=True)
-    ops.swap_blocks(buf, cache, m, stream_tensor=cache)
+    ops.swap_blocks(buf, cache, _pairs(np.arange(len(ids)), ids, cache.device), stream_tensor=cache)
+
+
+def _clone(pool: LocalPool) -> LocalPool:
+    """A copy whose later allocations and removals leave `pool` unchanged
+    (the per-sequence id lists are replaced, never edited, so they are
+    shared)."""
+    q = copy.copy(pool)
+    q.free = list(pool.free)
+    q.tables = dict(pool.tables)
+    q.lens = dict(pool.lens)
+    return q
 
 
 class MigrationError(RuntimeError):
@@ -249,17 +261,21 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
     before the deadline, e.g. because the peer exited).  On success the receivers scatter the slices into
     blocks allocated from their own pools and every rank applies the moves to
     `pools`.  Returns {"blocks_sent", "blocks_received", "bytes_sent",
-    "bytes_received"} for this rank (K and V).
+    "bytes_received", "device_ms", "host_ms"} for this rank (K and V;
+    device_ms: CUDA events on the current stream from the first gather to
+    the last scatter, None for CPU caches; host_ms: the whole call).
 
     gather / scatter move blocks between a cache and a contiguous staging
     buffer; the defaults are the library's CUDA kernels.
     """
     import torch
 
+    t_host = time.perf_counter()
     transport = transport or P2PTransport()
-    # the new bookkeeping, applied to a copy first: destination ids are
-    # allocated in move order, identically on every rank
-    new = copy.deepcopy(pools)
+    # the new bookkeeping, applied to copies of the pools the moves touch:
+    # destination ids are allocated in move order, identically on every rank
+    touched = {r for _, a, b in moves for r in (a, b)}
+    new = [(_clone(p) if r in touched else p) for r, p in enumerate(pools)]
     src_ids, dst_ids = {}, {}
     for seq, src, dst in moves:
         src_ids[seq] = list(new[src].tables[seq])
@@ -272,8 +288,12 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
     in_moves = [m for m in moves if m[2] == rank and m[1] != rank]
     sends, recvs, incoming = [], [], []
     n_out = sum(len(src_ids[s]) for s, _, _ in out_moves)
+    timed = k_cache.is_cuda
+    if timed:
+        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        ev[0].record()
     if n_out:
-        ids = [b for s, _, _ in out_moves for b in src_ids[s]]
+        ids = np.fromiter((b for s, _, _ in out_moves for b in src_ids[s]), np.int64, n_out)
         kb = torch.empty((n_out,) + tail, dtype=k_cache.dtype, device=k_cache.device)
         vb = torch.empty_like(kb)
         gather(k_cache, ids, kb)
@@ -289,7 +309,7 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
         kr = torch.empty((n,) + tail, dtype=k_cache.dtype, device=k_cache.device)
         vr = torch.empty_like(kr)
         recvs += [(kr, peer), (vr, peer)]
-        incoming.append((kr, vr, [b for s in seqs for b in dst_ids[s]]))
+        incoming.append((kr, vr, np.fromiter((b for s in seqs for b in dst_ids[s]), np.int64, n)))
     try:
         handles = transport.start(sends, recvs)
     except RuntimeError as e:  # e.g. the peer aborted or exited already
@@ -306,8 +326,15 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
                 tmp = torch.empty((len(src_ids[seq]),) + tail, dtype=cache.dtype, device=cache.device)
                 gather(cache, src_ids[seq], tmp)
                 scatter(tmp, cache, dst_ids[seq])
+    device_ms = None
+    if timed:
+        ev[1].record()
+        ev[1].synchronize()
+        device_ms = ev[0].elapsed_time(ev[1])
     for p, q in zip(pools, new):
-        p.__dict__.update(q.__dict__)
+        if p is not q:
+            p.__dict__.update(q.__dict__)
     n_in = sum(len(ids) for _, _, ids in incoming)
     return {"blocks_sent": n_out, "blocks_received": n_in, "bytes_sent": 2 * n_out * block_bytes,
-            "bytes_received": 2 * n_in * block_bytes}
+            "bytes_received": 2 * n_in * block_bytes, "device_ms": device_ms,
+            "host_ms": (time.perf_counter() - t_host) * 1e3}

@@ -9,6 +9,7 @@ import time
 
 import numpy as np
 import pytest
+import torch
 
 from cacheflow_b200 import sharding
 
@@ -66,11 +67,11 @@ def _free_port():
 
 
 def _cpu_gather(cache, ids, out):
-    out.copy_(cache[ids])
+    out.copy_(cache[torch.as_tensor(np.asarray(ids, np.int64))])
 
 
 def _cpu_scatter(buf, cache, ids):
-    cache[ids] = buf
+    cache[torch.as_tensor(np.asarray(ids, np.int64))] = buf
 
 
 def _migration_worker(rank, world, port, result_dir):
