@@ -414,9 +414,9 @@ struct TcLayout {
   static constexpr int kStage = 2 * kKBytes;          // K, then V
   static constexpr int kRingOff = kTcTiles * kQBytes;
   static constexpr int kBarOff = kRingOff + kTcStages * kStage;
-  // kv_full, kv_empty per stage; s_full per tile and S buffer; p_full,
+  // kv_full, kv_empty per stage; s_full and p_full per tile and S buffer;
   // o_done per tile; fin
-  static constexpr int kNumBars = 2 * kTcStages + 4 * kTcTiles + 1;
+  static constexpr int kNumBars = 2 * kTcStages + 5 * kTcTiles + 1;
   static constexpr int kMaskOff = kBarOff + kNumBars * 8;
   static constexpr int kTmemOff = kMaskOff + kTcStages * 4;
   static constexpr int kBytes = kTmemOff + 16;
@@ -465,8 +465,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + kTcStages;
   uint64_t* s_full = bars + 2 * kTcStages;  // per tile and S buffer: [2 x + buf]
-  uint64_t* p_full = s_full + 2 * kTcTiles; // per tile
-  uint64_t* o_done = p_full + kTcTiles;     // per tile
+  uint64_t* p_full = s_full + 2 * kTcTiles; // per tile and S buffer: [2 x + buf]
+  uint64_t* o_done = p_full + 2 * kTcTiles; // per tile
   uint64_t* fin = o_done + kTcTiles;
   int* vmask = reinterpret_cast<int*>(smem + L::kMaskOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemOff);
@@ -481,7 +481,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int x = 0; x < kTcTiles; ++x) {
       mbar_init(smem_addr(&s_full[2 * x]), 1);
       mbar_init(smem_addr(&s_full[2 * x + 1]), 1);
-      mbar_init(smem_addr(&p_full[x]), 4 * 32);
+      mbar_init(smem_addr(&p_full[2 * x]), 4 * 32);
+      mbar_init(smem_addr(&p_full[2 * x + 1]), 4 * 32);
       mbar_init(smem_addr(&o_done[x]), 1);
     }
     mbar_init(smem_addr(fin), 1);
@@ -581,29 +582,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
-      const uint32_t q_base = smem_addr(smem);
+      // Shared-memory descriptors: built once from the base addresses; an
+      // operand at byte offset o further on is the base descriptor + o / 16
+      // (the 14-bit address field holds any shared-memory address / 16, so
+      // the addition never carries out of it).
+      const uint64_t q_desc = smem_desc_sw128(smem_addr(smem), 16, 1024);
+      const uint64_t k_desc = smem_desc_sw128(smem_addr(smem + L::kRingOff), 16, 1024);
+      const uint64_t v_desc = smem_desc_sw128(smem_addr(smem + L::kRingOff + L::kKBytes), L::kKVBox, 1024);
       auto issue_qk = [&](int st, int x) {
-        const uint32_t kb = smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage);
-        const uint32_t qb = q_base + x * L::kQBytes;
+        const uint64_t qd = q_desc + (uint64_t)((x * L::kQBytes) >> 4);
+        const uint64_t kd = k_desc + (uint64_t)(((st % kTcStages) * L::kStage) >> 4);
         const uint32_t d = tmem + x * kTcTileCols + (st & 1) * kTcSCols;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(qb + (kk >> 2) * L::kQBox + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(kb + (kk >> 2) * L::kKVBox + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = qd + (uint64_t)(((kk >> 2) * L::kQBox + (kk & 3) * 32) >> 4);
+          const uint64_t bd = kd + (uint64_t)(((kk >> 2) * L::kKVBox + (kk & 3) * 32) >> 4);
           tc_mma_f16(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_addr(&s_full[2 * x + (st & 1)]));
       };
       auto issue_pv = [&](int st, int x) {
-        const uint32_t vb =
-            smem_addr(smem + L::kRingOff + (size_t)(st % kTcStages) * L::kStage + L::kKBytes);
+        const uint64_t vd = v_desc + (uint64_t)(((st % kTcStages) * L::kStage) >> 4);
         const uint32_t pt = tmem + x * kTcTileCols + (st & 1) * kTcSCols;  // P of this stage
         const uint32_t d = tmem + x * kTcTileCols + kTcOCol;
 #pragma unroll
         for (int j = 0; j < kStageBlocks; ++j) {
 #pragma unroll
           for (int hl = 0; hl < (kSplitP ? 2 : 1); ++hl) {
-            const uint64_t bd = smem_desc_sw128(vb + j * kBoxBytes, L::kKVBox, 1024);
+            const uint64_t bd = vd + (uint64_t)((j * kBoxBytes) >> 4);
             tc_mma_f16_ts(d, pt + hl * (kTcSCols / 2) + j * 8, bd, kIdescPV, (st > 0 || j > 0 || hl > 0) ? 1u : 0u);
           }
         }
@@ -632,7 +638,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int x = 0; x < kTcTiles; ++x) {
           // P of this tile written (and its S read): PV, then the S two
           // stages on.
-          if (!mbar_wait_bounded(smem_addr(&p_full[x]), (uint32_t)st & 1u)) {
+          // P of stage st arrives on the tile's barrier of S buffer st & 1,
+          // whose k-th completion (k = st / 2) is stage st: the softmax can
+          // be at most one stage ahead of this wait (its stage st + 2 needs
+          // QK(st + 2), issued after this PV), so the parity is unambiguous.
+          if (!mbar_wait_bounded(smem_addr(&p_full[2 * x + (st & 1)]), (uint32_t)(st >> 1) & 1u)) {
             ok = false;
             break;
           }
@@ -731,16 +741,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const float ps = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
       l_run = l_run * alpha + ps;
-      if (st > 0) {
-        // This tile's previous PV writes O (and read the other S buffer,
-        // which the next QK overwrites): wait for it.
+      if (st > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // A row of this warp rescales O: the tile's previous PV, which
+        // writes O, must be done.  Only then: the buffer this stage's P
+        // overwrites was last read by PV(st - 2), which finished before
+        // QK(st) wrote S(st) (the tensor pipe runs a thread's MMAs in
+        // order).  Skipped waits leave the parity unambiguous: PV(st) needs
+        // this stage's P, so o_done has completed st - 1 or st phases here.
         const bool r3 = mbar_wait_bounded(smem_addr(&o_done[x]), (uint32_t)(st - 1) & 1u);
         if (!__all_sync(0xffffffffu, r3)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             float o[32];
@@ -793,10 +807,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(smem_addr(&p_full[x]));
+      mbar_arrive(smem_addr(&p_full[2 * x + (st & 1)]));
     }
     if (ok) {
-      const bool r4 = mbar_wait_bounded(smem_addr(&o_done[x]), (uint32_t)(nstages - 1) & 1u);
+      // The last PV done: `fin` completes once, after every MMA of the CTA
+      // (o_done could be one or two phases short here, which its parity
+      // cannot tell apart).
+      const bool r4 = mbar_wait_bounded(smem_addr(fin), 0u);
       if (__all_sync(0xffffffffu, r4)) {
         tc_fence_after();
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
