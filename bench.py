@@ -538,6 +538,12 @@ def rebalance_check(full, parts, rank: int, world: int, k_cache, v_cache) -> dic
             g = torch.Generator(device=dev).manual_seed(777 + rank)
             qq = torch.empty((len(seqs), H, full.head_dim), dtype=qdt, device=dev).normal_(0, full.std, generator=g)
             out_seqs[peer] = (seqs, qq, attend(pools[rank], seqs, qq))
+    # NCCL connects a pair of ranks at its first point-to-point transfer (a
+    # one-time cost per process): connect the pairs the moves use first
+    pairs = sorted({(a, b) for _, a, b in moves if a != b})
+    tr = sharding.P2PTransport()
+    tr.wait(tr.start([(torch.zeros(1, device=dev), b) for a, b in pairs if a == rank],
+                     [(torch.empty(1, device=dev), a) for a, b in pairs if b == rank]), 60.0)
     torch.cuda.synchronize(dev)
     dist.barrier()
     stats = sharding.migrate(moves, rank, pools, k_cache, v_cache, timeout_s=60.0)
@@ -555,7 +561,6 @@ def rebalance_check(full, parts, rank: int, world: int, k_cache, v_cache) -> dic
             oo = torch.empty_like(qq)
             recvs += [(qq, peer), (oo, peer)]
             checks.append((seqs, qq, oo))
-    tr = sharding.P2PTransport()
     tr.wait(tr.start(sends, recvs), 60.0)
     verified = mismatched = 0
     for seqs, qq, oo in checks:
@@ -582,9 +587,10 @@ def rebalance_check(full, parts, rank: int, world: int, k_cache, v_cache) -> dic
         "sequences_verified": verified,
         "bitwise_equal": mismatched == 0 and errs == 0,
         "how": ("seeded finishes (rank r loses 0.4*r/(N-1) of its sequences), plan_rebalance to 2 %, "
-                "migrate(): block-copy gather, NCCL send/recv into the receiver's HBM, scatter; ms = CUDA events "
-                "from the first gather to the last scatter on each rank, max over ranks (host_ms: the whole "
-                "call, bookkeeping included); moved sequences' attention recomputed on the receiver"),
+                "migrate(): block-copy gather, NCCL send/recv into the receiver's HBM, scatter (rank pairs connected "
+                "beforehand by a 1-element exchange); ms = CUDA events from the first gather to the last scatter "
+                "on each rank, max over ranks (host_ms: the whole call, bookkeeping included); moved sequences' "
+                "attention recomputed on the receiver"),
     }
 
 
