@@ -241,6 +241,38 @@ def time_pool_ops(w, k_cache, v_cache, world: int, swap_gb: float):
     return res
 
 
+def workload_config(args, w, world: int, scaling: str, seqs_total: int) -> dict:
+    """The `config` of the bench line: the workload this rank's share runs
+    (both arms print the same dict; implementation choices of this library
+    go to `impl_config`)."""
+    fp8 = args.kv_dtype == "fp8"
+    kv_step = (w.kv_bytes() // w.elem_bytes if fp8 else
+               (w.chunked_kv_bytes() if w.has_chunks and args.prefill == "chunked" else w.kv_bytes()))
+    flush = w.kv_bytes() < 4 * L2_BYTES
+    return {
+        "workload": w.name,
+        "num_seqs_per_gpu": w.num_seqs,
+        "num_seqs_total": int(seqs_total),
+        "num_heads": w.num_heads,
+        "num_kv_heads": w.num_kv_heads,
+        "head_dim": w.head_dim,
+        "block_size": 16,
+        "context_lens": "min %d / mean %.0f / max %d" % (w.context_lens.min(), w.context_lens.mean(),
+                                                          w.context_lens.max()),
+        "pool_blocks_per_gpu": w.num_blocks,
+        "kv_dtype": "fp8 e4m3" if fp8 else w.dtype,
+        "kv_bytes_per_step_per_gpu": kv_step,
+        "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes() // (w.elem_bytes if fp8 else 1),
+        "l2": ("L2 flushed before every timed step (512 MB write, then a 512 MB read of a clean buffer; outside "
+               "the step's events)" if flush and args.l2_clean == "on" else
+               "L2 flushed before every timed step (512 MB write, outside the step's events)" if flush else
+               "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (kv_step / 1e9)),
+        "parallelism": (f"dp{world} (one global batch, sequences dealt to per-GPU pools by LPT)"
+                        if scaling == "strong" else
+                        f"dp{world} (per-GPU pools and batches, no data-path collective)"),
+    }
+
+
 def measure(args, w, rank: int, world: int, dev, kernel: str, steps: int, warmup: int, e2e: bool = True,
             post=None) -> dict:
     """Times `steps` decode steps of workload `w` on this rank (after `warmup`
@@ -665,18 +697,8 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": DTYPE_NAME[w.dtype],
             "data": "synthetic (seeded N(0,%g) caches, shapes of the workload)" % w.std,
-            "config": {
-                "workload": w.name,
-                "num_seqs_per_gpu": S,
-                "num_seqs_total": int(seqs_total),
-                "num_heads": H,
-                "num_kv_heads": Hkv,
-                "head_dim": D,
-                "block_size": 16,
-                "context_lens": "min %d / mean %.0f / max %d" % (w.context_lens.min(), w.context_lens.mean(),
-                                                                  w.context_lens.max()),
-                "pool_blocks_per_gpu": w.num_blocks,
-                "kv_bytes_per_step_per_gpu": kv_step,
+            "config": workload_config(args, w, world, scaling, seqs_total),
+            "impl_config": {
                 "prefill": ("chunked: %d decode rows + %d chunks through the multi-query operator"
                             % (chunks[0], chunks[1]) if r["chunked"] else
                             ("one decode row per prefill token" if w.has_chunks else None)),
@@ -685,17 +707,8 @@ def run_ours(args):
                 "v1_split": args.v1_split,
                 "append": ("new K/V appended inside the attention launch" if r["fused"]
                            else "reshape_and_cache launch before attention"),
-                "kv_dtype": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % r["kv_scale"]
+                "kv_cache": ("fp8 e4m3, per-cache scale %g (f16 tensor-core / f32 FMA arithmetic)" % r["kv_scale"]
                              if fp8 else w.dtype),
-                "l2": (("L2 flushed before every timed step (512 MB write, then a 512 MB read of a clean buffer; "
-                        "outside the step's events)" if r["flush_clean"] else
-                        "L2 flushed before every timed step (512 MB write, outside the step's events)")
-                       if r["flush"] else
-                       "inputs larger than L2 (%.2f GB of KV read per step per GPU vs 126 MB L2)" % (kv_step / 1e9)),
-                "unique_kv_bytes_per_step_per_gpu": w.unique_kv_bytes() // (w.elem_bytes if fp8 else 1),
-                "parallelism": (f"dp{world} (one global batch, sequences dealt to per-GPU pools by LPT)"
-                                if scaling == "strong" else
-                                f"dp{world} (per-GPU pools and batches, no data-path collective)"),
             },
             "tokens_per_s": round(seqs_total / (ms_step * 1e-3), 1),
             "unique_kv_GBps": round(world * w.unique_kv_bytes() / (w.elem_bytes if fp8 else 1)
@@ -833,7 +846,11 @@ def run_reference(args):
     rank, world, local = dist_env()
     if rank != 0:
         return
-    w = workloads.make(args.workload, seed=1234)
+    # this rank's share of the workload, as the GPU arm's rank 0 runs it
+    w, scaling = rank_workload(args, 0, world)
+    seqs_total = workloads.make(args.workload, seed=1234,
+                                **({"num_seqs": args.num_seqs} if args.num_seqs else {})).num_seqs \
+        if scaling == "strong" else w.num_seqs * world
     cb = cpu_baseline(w, steps=args.steps, warmup=args.warmup, total_budget_s=args.cpu_total_seconds)
     line = {
         "metric": METRIC,
@@ -844,12 +861,11 @@ def run_reference(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "strong" if args.workload in SHARDED else "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded N(0,%g))" % w.std,
-        "config": {"workload": w.name, "num_seqs_per_gpu": w.num_seqs, "num_heads": w.num_heads,
-                   "num_kv_heads": w.num_kv_heads, "head_dim": w.head_dim, "block_size": 16},
+        "data": "synthetic (seeded N(0,%g) caches, shapes of the workload)" % w.std,
+        "config": workload_config(args, w, world, scaling, seqs_total),
         "tokens_per_s": cb["tokens_per_s"],
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
