@@ -79,3 +79,63 @@ def test_sequence_migration_over_nccl(cflib, tmp_path):
         pytest.skip("needs 2 GPUs")
     mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
     assert (tmp_path / "ok").read_text() == "1"
+
+
+def _worker_both_ways(rank, world, port, result_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from cacheflow_b200 import ops, sharding
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        rng = np.random.default_rng(11)
+        ctx = rng.integers(30, 6000, 24)
+        pools = sharding.shard_workload(ctx, world, pool_factor=3.0, rng=np.random.default_rng(12))
+        nb = max(p.num_blocks for p in pools)
+        g = torch.Generator(device=dev).manual_seed(200 + rank)
+        k = torch.randn((nb, 8, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn((nb, 8, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+        # three sequences each way in one call
+        out0 = sorted(pools[0].tables, key=lambda s: -pools[0].lens[s])[:3]
+        out1 = sorted(pools[1].tables, key=lambda s: pools[1].lens[s])[:3]
+        moves = [(s, 0, 1) for s in out0] + [(s, 1, 0) for s in out1]
+        mine = out0 if rank == 0 else out1
+        qg = torch.Generator(device=dev).manual_seed(7)
+        q = torch.randn((1, 32, 128), generator=qg, device=dev).to(torch.bfloat16)
+        for s in mine:
+            torch.save(_attend_one(ops, pools[rank], s, k, v, q).cpu(), os.path.join(result_dir, f"b{s}.pt"))
+        stats = sharding.migrate(moves, rank, pools, k, v, timeout_s=60.0)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        got = out1 if rank == 0 else out0
+        ok = stats["device_ms"] is not None and stats["blocks_received"] == sum(
+            (pools[rank].lens[s] + 15) // 16 for s in got)
+        for s in got:
+            after = _attend_one(ops, pools[rank], s, k, v, q).cpu()
+            ok = ok and torch.equal(after, torch.load(os.path.join(result_dir, f"b{s}.pt")))
+        ok = ok and ops.device_errors(rank) == 0
+        with open(os.path.join(result_dir, f"ok{rank}"), "w") as f:
+            f.write("1" if ok else "0")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_migration_both_ways_over_nccl(cflib, tmp_path):
+    """Six sequences, three each way, in one migrate() call: one batched NCCL
+    group, deadline-bounded wait, attention bitwise unchanged on both ranks."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_worker_both_ways, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    assert (tmp_path / "ok0").read_text() == "1" and (tmp_path / "ok1").read_text() == "1"
