@@ -672,11 +672,15 @@ def run_ours(args):
     kv_step = r["kv_step"]
     times = torch.tensor([ms_step, att_ms, e2e_ms], dtype=torch.float64, device=dev)
     totals = torch.tensor([kv_step, S], dtype=torch.float64, device=dev)
+    # per-rank spread: what limits the scaling (the slowest rank sets the step)
+    spread = torch.tensor([att_ms, kv_step, -att_ms, -kv_step], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
+        dist.all_reduce(spread, op=dist.ReduceOp.MAX)
     ms_step, att_ms, e2e_ms = times.tolist()
     kv_total, seqs_total = totals.tolist()
+    k_max, b_max, k_min, b_min = spread[0].item(), spread[1].item(), -spread[2].item(), -spread[3].item()
 
     if rank == 0:
         peak, peak_kind = hbm_peak()
@@ -742,6 +746,15 @@ def run_ours(args):
             "gpu_launches": r["launches_per_step"] * args.steps,
             "clocks": r["clocks"],
         }
+        if world > 1:
+            line["ranks"] = {
+                "kernel_ms_min": round(k_min, 4),
+                "kernel_ms_max": round(k_max, 4),
+                "kv_bytes_max_over_mean": round(b_max / (kv_total / world), 6),
+                "kv_bytes_min_over_mean": round(b_min / (kv_total / world), 6),
+                "note": ("the step is the slowest rank's; spread of the attention launch time and of the KV "
+                         "bytes each rank reads"),
+            }
         if pool_ops is not None:
             line["pool_ops_rank0"] = pool_ops
         if "migration" in r["post"]:
