@@ -1085,6 +1085,74 @@ __global__ void __launch_bounds__(kReduceThreads) paged_attention_reduce_kernel(
   }
 }
 
+// Partition reduce for launches of at most 32 partitions (v1 splits of
+// ordinary contexts): one warp per (query head, sequence), eight heads per
+// CTA.  Lane p holds partition p's max and weight (one round of loads, warp
+// shuffles for the max and the sum), then every lane accumulates its float4
+// column slices over the partitions with the loads pipelined -- no shared
+// memory, no CTA barrier.  Same merge as paged_attention_reduce_kernel:
+// out = sum_p w_p o_p / sum_p w_p, w_p = exp_sum_p * exp(max_p - max).
+constexpr int kReduceRowWarps = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kReduceRowWarps * 32) paged_attention_reduce_rows_kernel(const ReduceArgs r) {
+  constexpr int kCols4 = D / 4;
+  constexpr int kPerLane = (kCols4 + 31) / 32;
+  grid_dependency_wait();
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x * kReduceRowWarps + (threadIdx.x >> 5);
+  const int seq = blockIdx.y;
+  if (h >= r.num_heads) return;
+  int ctx = r.context_lens[seq];
+  const int cap = r.max_blocks_per_seq * kBlockTokens;
+  ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
+  const int nblk = (ctx + kBlockTokens - 1) / kBlockTokens;
+  int nparts = nblk == 0 ? 1 : (nblk + r.part_blocks - 1) / r.part_blocks;
+  if (nparts <= 1) return;  // written by the partition kernel
+  if (nparts > r.launched_parts) nparts = r.launched_parts;
+  const size_t base = ((size_t)seq * r.num_heads + h) * r.num_parts;
+  const float pm = lane < nparts ? r.part_max[base + lane] : -INFINITY;
+  const float ps = lane < nparts ? r.part_sum[base + lane] : 0.f;
+  float M = pm;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float w = (lane < nparts && M != -INFINITY) ? ps * expf(pm - M) : 0.f;
+  float L = w;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  const float4* po = reinterpret_cast<const float4*>(r.part_out + base * D);
+  float4 acc[kPerLane];
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int p = 0; p < nparts; ++p) {
+    const float wp = __shfl_sync(0xffffffffu, w, p);
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+      const int c4 = lane + 32 * k;
+      if (c4 < kCols4) {
+        const float4 v = po[(size_t)p * kCols4 + c4];
+        acc[k].x = fmaf(wp, v.x, acc[k].x);
+        acc[k].y = fmaf(wp, v.y, acc[k].y);
+        acc[k].z = fmaf(wp, v.z, acc[k].z);
+        acc[k].w = fmaf(wp, v.w, acc[k].w);
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  T* out = reinterpret_cast<T*>(r.out) + ((size_t)seq * r.num_heads + h) * D;
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) {
+    const int c4 = lane + 32 * k;
+    if (c4 < kCols4) {
+      out[c4 * 4 + 0] = from_float<T>(acc[k].x * inv);
+      out[c4 * 4 + 1] = from_float<T>(acc[k].y * inv);
+      out[c4 * 4 + 2] = from_float<T>(acc[k].z * inv);
+      out[c4 * 4 + 3] = from_float<T>(acc[k].w * inv);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
@@ -1180,15 +1248,20 @@ cf_status launch_typed(const AttnLaunch& l, AttnArgs a, int grid_x, const Maps& 
   if (rsmem > 48 * 1024) return CF_ERR_UNSUPPORTED;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
-  cfg.blockDim = dim3(kReduceThreads);
-  cfg.dynamicSmemBytes = rsmem;
   cfg.stream = l.stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (grid_x <= 32) {  // a warp per (head, sequence): one lane per partition
+    cfg.gridDim = dim3((unsigned)((p.num_heads + kReduceRowWarps - 1) / kReduceRowWarps), (unsigned)p.num_seqs);
+    cfg.blockDim = dim3(kReduceRowWarps * 32);
+    return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_reduce_rows_kernel<T, D>, r));
+  }
+  cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
+  cfg.blockDim = dim3(kReduceThreads);
+  cfg.dynamicSmemBytes = rsmem;
   return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_reduce_kernel<T, D>, r));
 }
 
