@@ -47,13 +47,19 @@ int32_t v1_split_tokens(const cf_paged_attention_params* p) {
     return (int32_t)-1;
   }();
   if (forced >= 0) return forced;
-  // 1024-token partitions, or 2048 past 8192 tokens (a long context then
-  // writes and merges a quarter of the partial results of v2's 512-token
-  // partitions: 0.589 vs 0.639 ms on 16 rows of 16K-128K tokens), halved
-  // down to 512 while that is needed for about four CTAs per SM.
+  // Partitions of 2048 tokens, 4096 past 8192 tokens, and 8192 when such a
+  // batch also has 4096 or more (row, KV head) pairs; halved down to 512
+  // while that is needed for about four CTAs per SM.  Longer partitions mean
+  // fewer CTAs (each with its own set-up and merge) and fewer partial results
+  // to write and merge; shorter ones a shorter tail.  Measured (attention
+  // launch, bf16, 8 KV heads): 1024 rows of 512-32K tokens 9.71 / 9.78 /
+  // 9.99 ms at 8192 / 4096 / 2048; 128 such rows 1.362 / 1.356 / 1.366 ms;
+  // 16 rows of 16K-128K tokens 0.619 / 0.589 / 0.594 ms; 64 rows of
+  // 128-4096 tokens (32 KV heads) 0.336 / 0.339 / 0.340 ms at 2048 / 1024 /
+  // unsplit.
   constexpr int64_t kTargetCtas = 4 * 148;
   const int64_t pairs = (int64_t)p->num_seqs * p->num_kv_heads;
-  int32_t split = p->max_context_len > 8192 ? 2048 : 1024;
+  int32_t split = p->max_context_len > 8192 ? (pairs >= 4096 ? 8192 : 4096) : 2048;
   while (split > 512 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
   return split;
 }
@@ -223,7 +229,17 @@ const char* cf_status_string(cf_status status) {
 
 size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) {
   if (check_attention_params(p, /*check_pointers=*/false) != CF_OK) return 0;
-  return v1_split_bytes(p, nullptr);
+  // Enough for every call with these sizes and any shorter max_context_len
+  // (a host sizes the workspace once, for its longest context): the split
+  // grows with the context, so a shorter context can need more partitions.
+  cf_paged_attention_params q = *p;
+  size_t bytes = v1_split_bytes(p, nullptr);
+  for (int64_t c = 512; c < p->max_context_len; c += 512) {
+    q.max_context_len = (int32_t)c;
+    const size_t b = v1_split_bytes(&q, nullptr);
+    bytes = b > bytes ? b : bytes;
+  }
+  return bytes;
 }
 
 cf_status cf_paged_attention_v1(const cf_paged_attention_params* p, void* workspace,

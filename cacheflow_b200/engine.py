@@ -9,8 +9,8 @@ same host-side batch description is staged into device buffers owned by the
 engine, the new K/V rows are scattered into the cache, attention runs on the
 device, and the output is copied back.  Attention runs v1 with the
 library's own context split for every length (kernel="v1", the default:
-2048-token partitions past 8192 tokens write a quarter of v2's partial
-results), or follows the reference's choice (kernel="reference": v1 when the
+4096- or 8192-token partitions past 8192 tokens write an eighth or less of
+v2's partial results), or follows the reference's choice (kernel="reference": v1 when the
 longest context is at most 8192 tokens, else v2 with 512-token partitions,
 :162-177).
 

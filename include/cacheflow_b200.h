@@ -94,7 +94,9 @@ CF_API cf_status cf_paged_attention_v1(const cf_paged_attention_params* params,
                                 void* stream);
 
 /* Bytes of workspace the split path of cf_paged_attention_v1 uses for these
- * params (depends only on host-side fields); 0 means it never splits. */
+ * params, or for the same sizes with any shorter max_context_len (a host
+ * sizes the workspace once for its longest context); depends only on
+ * host-side fields; 0 means it never splits. */
 CF_API size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* params);
 
 /* Partitioned decode attention: partitions of 512 tokens, then an exp-sum/max

@@ -186,7 +186,7 @@ def test_v1_workspace_size_needs_shapes_only(cflib):
     p.num_seqs, p.num_heads, p.num_kv_heads, p.head_dim, p.block_size = 64, 32, 32, 128, 16
     p.max_context_len, p.max_blocks_per_seq, p.dtype = 4096, 256, _lib.CF_F16
     n = cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p))
-    parts = 4096 // 1024
+    parts = 4096 // 2048
     rows = 64 * 32 * parts
     assert n >= rows * (128 + 2) * 4
     p.max_context_len = 1000  # fits one partition: never splits
@@ -199,8 +199,10 @@ def _split_bytes(rows, D):
 
 
 def test_v1_split_policy(cflib):
-    """Partitions of 1024 tokens, 2048 past 8192 tokens, halved (not below
-    512) while the grid would hold fewer than ~4 CTAs per SM of 148."""
+    """Partitions of 2048 tokens, 4096 past 8192 tokens (8192 with 4096 or more
+    row x KV head pairs), halved (not below 512) while the grid would hold
+    fewer than ~4 CTAs per SM of 148; the workspace covers every shorter
+    context too."""
     import os
 
     from cacheflow_b200 import _lib
@@ -209,15 +211,26 @@ def test_v1_split_policy(cflib):
         pytest.skip("CF_V1_SPLIT_TOKENS overrides the policy")
     p = _lib.AttentionParams()
     p.num_heads, p.head_dim, p.block_size, p.dtype = 32, 128, 16, _lib.CF_BF16
-    # 16 rows x 8 kv heads up to 124,872 tokens: 2048-token partitions (61)
+    size = lambda: cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p))  # noqa: E731
+    # 16 rows x 8 kv heads up to 124,872 tokens: 4096-token partitions (31)
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 16, 8, 124872, 7805
-    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(16 * 32 * 61, 128)
-    # 64 rows x 32 kv heads up to 4096 tokens: 1024-token partitions (4)
+    assert size() == _split_bytes(16 * 32 * 31, 128)
+    # 64 rows x 32 kv heads up to 4096 tokens: 2048-token partitions (2)
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 64, 32, 4096, 256
-    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(64 * 32 * 4, 128)
-    # 2 rows x 8 kv heads up to 20,000 tokens: 2048 gives 160 CTAs, 1024 320, 512 640
+    assert size() == _split_bytes(64 * 32 * 2, 128)
+    # 2 rows x 8 kv heads up to 20,000 tokens: 4096 gives 80 CTAs ... 512 640
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 2, 8, 20000, 1250
-    assert cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p)) == _split_bytes(2 * 32 * 40, 128)
+    assert size() == _split_bytes(2 * 32 * 40, 128)
+    # 1024 rows x 8 kv heads (8192 pairs) up to 32,659 tokens: 8192-token partitions (4)
+    p.num_heads = 64
+    p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 1024, 8, 32659, 2042
+    assert size() == _split_bytes(1024 * 64 * 4, 128)
+    # 16 rows x 8 kv heads up to 10,000 tokens: the call itself needs 5
+    # partitions (4096 -> 2048), one of 8192 tokens 8 (2048 -> 1024): the
+    # workspace is sized for 8
+    p.num_heads = 32
+    p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 16, 8, 10000, 625
+    assert size() == _split_bytes(16 * 32 * 8, 128)
 
 
 def test_engine_rejects_unknown_kernel_choice_before_touching_a_gpu():

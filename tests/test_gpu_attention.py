@@ -89,7 +89,8 @@ def test_v1_split_matches_oracle(cflib, oracle_mod, monkeypatch, dtype, H, Hkv, 
     host, d = _setup(rng, dtype, H, Hkv, D, ctx)
     scale = 1.0 / math.sqrt(D)
     n = ops.paged_attention_v1_workspace_size(d["q"], d["k"], d["bt"], max(ctx))
-    # partitions are 512 or 1024 tokens: longer contexts always split, shorter never
+    # these small batches split at 512 or 1024 tokens (the policy halves its
+    # 2048-token partitions to fill the GPU): longer contexts always split
     if max(ctx) > 1024:
         assert n > 0
     if max(ctx) <= 512:
