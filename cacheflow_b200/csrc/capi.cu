@@ -38,7 +38,7 @@ constexpr int32_t kV2PartitionTokens = 512;  // CacheFlow's PARTITION_SIZE (page
 // steps in 34 us at 128- or 256-token partitions against 29 us unsplit).
 // 0 disables splitting; CF_V1_SPLIT_TOKENS (a multiple of 16; 0 = never)
 // overrides the choice.
-int32_t v1_split_tokens(const cf_paged_attention_params* p) {
+int32_t v1_split_tokens(const cf_paged_attention_params* p, bool fp8_cache) {
   static const int32_t forced = [] {
     if (const char* e = std::getenv("CF_V1_SPLIT_TOKENS")) {
       long x = std::strtol(e, nullptr, 10);
@@ -47,19 +47,21 @@ int32_t v1_split_tokens(const cf_paged_attention_params* p) {
     return (int32_t)-1;
   }();
   if (forced >= 0) return forced;
-  // Partitions of 2048 tokens, 4096 past 8192 tokens, and 8192 when such a
-  // batch also has 4096 or more (row, KV head) pairs; halved down to 512
-  // while that is needed for about four CTAs per SM.  Longer partitions mean
-  // fewer CTAs (each with its own set-up and merge) and fewer partial results
-  // to write and merge; shorter ones a shorter tail.  Measured (attention
-  // launch, bf16, 8 KV heads): 1024 rows of 512-32K tokens 9.71 / 9.78 /
-  // 9.99 ms at 8192 / 4096 / 2048; 128 such rows 1.362 / 1.356 / 1.366 ms;
-  // 16 rows of 16K-128K tokens 0.619 / 0.589 / 0.594 ms; 64 rows of
+  // Partitions of 2048 tokens, 4096 past 8192 tokens (2048 again for an fp8
+  // cache), and 8192 when such a batch also has 4096 or more (row, KV head)
+  // pairs; halved down to 512 while that is needed for about four CTAs per
+  // SM.  Longer partitions mean fewer CTAs (each with its own set-up and
+  // merge) and fewer partial results to write and merge; shorter ones a
+  // shorter tail.  Measured (attention launch, 8 KV heads, at 8192 / 4096 /
+  // 2048): bf16, 1024 rows of 512-32K tokens 9.71 / 9.78 / 9.99 ms; 128 such
+  // rows 1.362 / 1.356 / 1.366 ms; 16 rows of 16K-128K tokens 0.619 / 0.589
+  // / 0.594 ms; fp8, 1024 rows of 512-32K tokens 5.43 / 5.54 / 5.82 ms; 16
+  // rows of 16K-128K tokens 0.349 / 0.332 / 0.322 ms; 64 bf16 rows of
   // 128-4096 tokens (32 KV heads) 0.336 / 0.339 / 0.340 ms at 2048 / 1024 /
   // unsplit.
   constexpr int64_t kTargetCtas = 4 * 148;
   const int64_t pairs = (int64_t)p->num_seqs * p->num_kv_heads;
-  int32_t split = p->max_context_len > 8192 ? (pairs >= 4096 ? 8192 : 4096) : 2048;
+  int32_t split = p->max_context_len > 8192 ? (pairs >= 4096 ? 8192 : (fp8_cache ? 2048 : 4096)) : 2048;
   while (split > 512 && pairs * ((p->max_context_len + split - 1) / split) < kTargetCtas) split /= 2;
   return split;
 }
@@ -114,7 +116,7 @@ cf_status check_attention_params(const cf_paged_attention_params* p, bool check_
   return CF_OK;
 }
 
-size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out);
+size_t v1_split_bytes(const cf_paged_attention_params* p, bool fp8_cache, int32_t* parts_out);
 
 // Launch extras beyond the attention params: the fused append's rows and an
 // fp8 cache's element type and scales.
@@ -144,13 +146,14 @@ cf_status run_v1(const cf_paged_attention_params* p, void* workspace, size_t wor
   AttnLaunch l{p, 0, 1, nullptr, nullptr, nullptr, (cudaStream_t)stream};
   apply(l, x);
   int32_t parts = 0;
-  const size_t need = v1_split_bytes(p, &parts);
+  const bool fp8_cache = x.cache_dtype == CF_FP8_E4M3;
+  const size_t need = v1_split_bytes(p, fp8_cache, &parts);
   if (need > 0 && workspace != nullptr && workspace_bytes >= need) {
     if (!aligned16(workspace)) return CF_ERR_INVALID_ARGUMENT;
     const int64_t rows = (int64_t)p->num_seqs * p->num_heads * parts;
     const int64_t r4 = (rows * 4 + 255) / 256 * 256;
     uint8_t* w = static_cast<uint8_t*>(workspace);
-    l.part_tokens = v1_split_tokens(p);
+    l.part_tokens = v1_split_tokens(p, fp8_cache);
     l.num_parts = parts;
     l.part_max = reinterpret_cast<float*>(w);
     l.part_sum = reinterpret_cast<float*>(w + r4);
@@ -193,8 +196,8 @@ Extras fp8_extras(float k_scale, float v_scale) {
   return x;
 }
 
-size_t v1_split_bytes(const cf_paged_attention_params* p, int32_t* parts_out) {
-  const int32_t split = v1_split_tokens(p);
+size_t v1_split_bytes(const cf_paged_attention_params* p, bool fp8_cache, int32_t* parts_out) {
+  const int32_t split = v1_split_tokens(p, fp8_cache);
   if (split <= 0 || p->num_seqs <= 0 || p->max_context_len <= split) return 0;
   const int64_t parts = (p->max_context_len + split - 1) / split;
   if (parts_out) *parts_out = (int32_t)parts;
@@ -232,12 +235,16 @@ size_t cf_paged_attention_v1_workspace_size(const cf_paged_attention_params* p) 
   // Enough for every call with these sizes and any shorter max_context_len
   // (a host sizes the workspace once, for its longest context): the split
   // grows with the context, so a shorter context can need more partitions.
+  // The params do not say whether the cache is fp8, so both policies count.
   cf_paged_attention_params q = *p;
-  size_t bytes = v1_split_bytes(p, nullptr);
-  for (int64_t c = 512; c < p->max_context_len; c += 512) {
-    q.max_context_len = (int32_t)c;
-    const size_t b = v1_split_bytes(&q, nullptr);
-    bytes = b > bytes ? b : bytes;
+  size_t bytes = 0;
+  for (int64_t c = 512;; c += 512) {
+    q.max_context_len = (int32_t)(c < p->max_context_len ? c : p->max_context_len);
+    for (bool fp8_cache : {false, true}) {
+      const size_t b = v1_split_bytes(&q, fp8_cache, nullptr);
+      bytes = b > bytes ? b : bytes;
+    }
+    if (c >= p->max_context_len) break;
   }
   return bytes;
 }

@@ -199,10 +199,10 @@ def _split_bytes(rows, D):
 
 
 def test_v1_split_policy(cflib):
-    """Partitions of 2048 tokens, 4096 past 8192 tokens (8192 with 4096 or more
-    row x KV head pairs), halved (not below 512) while the grid would hold
-    fewer than ~4 CTAs per SM of 148; the workspace covers every shorter
-    context too."""
+    """Partitions of 2048 tokens, 4096 past 8192 tokens (2048 for an fp8 cache,
+    8192 with 4096 or more row x KV head pairs), halved (not below 512) while
+    the grid would hold fewer than ~4 CTAs per SM of 148; the workspace covers
+    every shorter context and both cache types."""
     import os
 
     from cacheflow_b200 import _lib
@@ -212,9 +212,10 @@ def test_v1_split_policy(cflib):
     p = _lib.AttentionParams()
     p.num_heads, p.head_dim, p.block_size, p.dtype = 32, 128, 16, _lib.CF_BF16
     size = lambda: cflib.cf_paged_attention_v1_workspace_size(ctypes.byref(p))  # noqa: E731
-    # 16 rows x 8 kv heads up to 124,872 tokens: 4096-token partitions (31)
+    # 16 rows x 8 kv heads up to 124,872 tokens: 4096-token partitions (31),
+    # 2048 for an fp8 cache (61), which sets the size
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 16, 8, 124872, 7805
-    assert size() == _split_bytes(16 * 32 * 31, 128)
+    assert size() == _split_bytes(16 * 32 * 61, 128)
     # 64 rows x 32 kv heads up to 4096 tokens: 2048-token partitions (2)
     p.num_seqs, p.num_kv_heads, p.max_context_len, p.max_blocks_per_seq = 64, 32, 4096, 256
     assert size() == _split_bytes(64 * 32 * 2, 128)
