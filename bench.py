@@ -468,12 +468,42 @@ def measure(args, w, rank: int, world: int, dev, kernel: str, steps: int, warmup
         "attention_launches": len(att_ev),
         "h2d_bytes": engine.h2d_bytes(S, T), "d2h_bytes": engine.d2h_bytes(S),
     }
+    if flush is not None:
+        res["copy_same_traffic"] = cold_copy_time(stream, alg_bytes, flush, flush_clean)
     if post is not None:
         with torch.cuda.stream(stream):
             res["post"] = post(k_cache, v_cache)
     del engine, k_cache, v_cache, flush, flush_clean
     torch.cuda.empty_cache()
     return res
+
+
+def cold_copy_time(stream, traffic: int, flush, flush_clean, reps: int = 50) -> dict:
+    """A device copy moving the same DRAM traffic (half read, half written)
+    as one attention launch, timed like the steps of a batch that fits in L2
+    (L2 overwritten before each copy, events around the copy alone): what any
+    kernel can reach at this size from a cold L2."""
+    import torch
+
+    n = traffic // 2 // 16 * 16
+    src = torch.empty(n, dtype=torch.uint8, device=flush.device)
+    dst = torch.empty_like(src)
+    src.fill_(1)
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(reps + 5):
+            flush.zero_()
+            if flush_clean is not None:
+                flush_clean.max()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src)
+            b.record(stream)
+            times.append((a, b))
+    torch.cuda.synchronize(flush.device)
+    ms = sorted(a.elapsed_time(b) for a, b in times[5:])
+    med = ms[len(ms) // 2]
+    return {"bytes": 2 * n, "us": round(med * 1e3, 2), "GBps": round(2 * n / (med * 1e-3) / 1e9, 1)}
 
 
 def attention_kind(r: dict) -> str:
@@ -754,6 +784,13 @@ def run_ours(args):
                 "kv_bytes_min_over_mean": round(b_min / (kv_total / world), 6),
                 "note": ("the step is the slowest rank's; spread of the attention launch time and of the KV "
                          "bytes each rank reads"),
+            }
+        if "copy_same_traffic" in r:
+            c = r["copy_same_traffic"]
+            line["roofline"]["cold_copy_same_traffic"] = {
+                **c, "frac_of_peak": round(c["GBps"] / peak, 4), "kernel_over_copy": round(att_ms * 1e3 / c["us"], 3),
+                "note": ("a device copy of the launch's algorithmic bytes (half read, half written) timed like the "
+                         "step, L2 overwritten before each: the reachable rate at this size"),
             }
         if pool_ops is not None:
             line["pool_ops_rank0"] = pool_ops

@@ -795,7 +795,10 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
 
   Consumer cons;
   const T* qrow = reinterpret_cast<const T*>(a.q) + ((size_t)seq * a.num_heads + head0) * D;
-  cons.init(qrow, nheads, a.scale_log2, lane);
+  // The tensor-core consumers only load Q here; the FMA consumer scales it as
+  // it arrives, so it starts after the first copies are issued (below) and
+  // Q's memory round trip overlaps theirs.
+  if constexpr (kMma) cons.init(qrow, nheads, a.scale_log2, lane);
 
   // The partition's tiles (R tokens each, kSubs per block) are dealt to the
   // warps round-robin: this warp's tiles are u = warp + j*NW, j in [0, nb);
@@ -865,6 +868,7 @@ __global__ void __launch_bounds__(AttnConfig<TC, D, HG>::kWarps * 32, AttnConfig
     const int phys = __shfl_sync(0xffffffffu, ids, j);
     if (lane == 0) issue(j, phys);
   }
+  if constexpr (!kMma) cons.init(qrow, nheads, a.scale_log2, lane);
 
   // The streaming loop.  With kAppend the newest token's tile is the last
   // tile of the warp that holds it (the partition's highest tile, or the one
