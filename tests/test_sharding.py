@@ -128,6 +128,72 @@ def test_block_migration_two_gloo_ranks(tmp_path):
     assert (tmp_path / "ok1").read_text() == "1"
 
 
+def _four_rank_plan(world):
+    """The rebalancing round the bench runs at N > 1, on CPU: LPT shares,
+    rank r loses 0.4 * r / (N - 1) of its sequences, then plan_rebalance."""
+    ctx = np.random.default_rng(21).integers(20, 900, 48).astype(np.int64)
+    pools = sharding.shard_workload(ctx, world, pool_factor=3.0, rng=np.random.default_rng(5))
+    rng = np.random.default_rng(99)
+    for r, p in enumerate(pools):
+        seqs = sorted(p.tables)
+        for s in rng.choice(seqs, int(0.4 * r / (world - 1) * len(seqs)), replace=False):
+            p.remove_sequence(int(s))
+    moves = sharding.plan_rebalance([p.load() for p in pools], [p.lens for p in pools], tolerance=0.02)
+    return pools, moves
+
+
+def _many_peer_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    pools, moves = _four_rank_plan(world)
+    shape = (max(p.num_blocks for p in pools) + 64, 2, 16, 8)
+    g = torch.Generator().manual_seed(200 + rank)
+    k, v = torch.randn(shape, generator=g), torch.randn(shape, generator=g)
+    for s, a, b in moves:
+        if a == rank:
+            ids = pools[rank].tables[s]
+            torch.save((k[ids].clone(), v[ids].clone()), os.path.join(result_dir, f"seq{s}.pt"))
+    moved = {s for s, _, _ in moves}
+    stay = [s for s in pools[rank].tables if s not in moved]
+    before = {s: (k[pools[rank].tables[s]].clone(), v[pools[rank].tables[s]].clone()) for s in stay}
+    stats = sharding.migrate(moves, rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter, timeout_s=60)
+    dist.barrier()
+    ok = True
+    got = 0
+    for s, a, b in moves:
+        if b == rank:
+            sk, sv = torch.load(os.path.join(result_dir, f"seq{s}.pt"))
+            ids = pools[rank].tables[s]
+            ok = ok and torch.equal(k[ids], sk) and torch.equal(v[ids], sv)
+            got += len(ids)
+        ok = ok and (s in pools[b].tables) and (s not in pools[a].tables)
+    for s, (bk, bv) in before.items():
+        ok = ok and torch.equal(k[pools[rank].tables[s]], bk) and torch.equal(v[pools[rank].tables[s]], bv)
+    ok = ok and stats["blocks_received"] == got
+    with open(os.path.join(result_dir, f"ok{rank}"), "w") as f:
+        f.write("1" if ok else "0")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_block_migration_four_gloo_ranks_many_peers(tmp_path):
+    """plan_rebalance's moves between four ranks (several senders and
+    receivers, some ranks both) through one migrate() call per rank."""
+    import torch.multiprocessing as mp
+
+    _, moves = _four_rank_plan(4)
+    pairs = {(a, b) for _, a, b in moves}
+    assert len(moves) >= 3 and len(pairs) >= 2, moves
+    port = _free_port()
+    mp.start_processes(_many_peer_worker, args=(4, port, str(tmp_path)), nprocs=4, start_method="spawn")
+    for r in range(4):
+        assert (tmp_path / f"ok{r}").read_text() == "1", r
+
+
 class _DropSecondSend(sharding.P2PTransport):
     """Posts only the first of its sends: the V slice is lost on the way."""
 
