@@ -1,7 +1,7 @@
 /*
  * cf_oracle.c -- CPU restatement of CacheFlow's KV-cache kernel path.
  *
- * TEST INFRASTRUCTURE ONLY (the checker; see cf_oracle.h).  Nothing in the
+ * TEST INFRASTRUCTURE ONLY (the oracle; see cf_oracle.h).  Nothing in the
  * product links or calls this file.
  *
  * Reference lines followed (CacheFlow, src/cacheflow/cuda/):

@@ -1,7 +1,7 @@
 /*
  * cf_oracle.h -- CPU restatement of CacheFlow's KV-cache kernel path.
  *
- * TEST INFRASTRUCTURE ONLY.  This code is the checker: tests, the smoke test
+ * TEST INFRASTRUCTURE ONLY.  This code is the oracle: tests, the smoke test
  * and the CPU-baseline leg of bench.py call it to produce expected results.
  * The product (libcacheflow_b200.so) never links, loads or calls it.
  *

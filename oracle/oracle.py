@@ -2,7 +2,7 @@
 libraries under oracle/_ref/.
 
 TEST / BENCH INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke()
-and the CPU-baseline leg of bench.py as the checker.  The product package
+and the CPU-baseline leg of bench.py as the oracle.  The product package
 (cacheflow_b200) never imports this module.
 """
 
