@@ -822,47 +822,58 @@ def traffic_from_profiles(workload: str):
 # ---------------------------------------------------------------------------
 # CacheFlow's own CPU decode step on a bounded sample (reference arm / baseline).
 # ---------------------------------------------------------------------------
-def reference_sample(w: workloads.Workload, max_seqs: int):
-    """The first `max_seqs` rows of the workload with their blocks renumbered
-    into a compact fp32 pool (the reference is fp32-only)."""
+def reference_sample(w: workloads.Workload, max_seqs: int, max_tokens: int | None = None):
+    """The first `max_seqs` rows of the workload (each context cut to its
+    first `max_tokens` tokens, if given) with their blocks renumbered into a
+    compact fp32 pool (the reference is fp32-only)."""
     rows = np.arange(min(max_seqs, w.num_seqs))
-    ctx = w.context_lens[rows]
-    nblk = (ctx.astype(np.int64) + 15) // 16
+    ctx = w.context_lens[rows].astype(np.int64)
+    if max_tokens is not None:
+        ctx = np.minimum(ctx, max_tokens)
+    nblk = (ctx + 15) // 16
     tables = np.zeros((len(rows), int(nblk.max())), np.int32)
     remap = {}
     for i, r in enumerate(rows):
         for b in range(nblk[i]):
             old = int(w.block_tables[r, b])
             tables[i, b] = remap.setdefault(old, len(remap))
-    return ctx, tables, len(remap)
+    return ctx.astype(w.context_lens.dtype), tables, len(remap)
 
 
 def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | None = None, warmup: int = 1,
                  max_seqs: int = 16, total_budget_s: float | None = None):
     """CacheFlow's own CPU decode step on the first rows of `w`.  With
     `steps`, exactly that many timed steps run; total_budget_s then caps the
-    whole run (warm-up included) by shrinking the sample to fewer rows, found
-    from one probe step of the full sample.  Without `steps`, steps repeat for
-    about budget_s seconds."""
+    whole run (warm-up included) by cutting the sample's contexts shorter
+    (the rows stay, so every host thread keeps a sequence: the reference
+    step spreads sequences over its threads), found from one probe step;
+    only contexts already at 16 tokens make it drop rows.  Without `steps`,
+    steps repeat for about budget_s seconds."""
     from oracle import oracle
 
     threads = os.cpu_count() or 1
     n = min(w.num_seqs, max_seqs)
+    cap = None
     while True:
-        ctx, tables, pool = reference_sample(w, n)
+        ctx, tables, pool = reference_sample(w, n, cap)
         ref = oracle.RefCpu(w.num_heads, w.num_kv_heads, w.head_dim, pool, threads)
         k, v = ref.caches()
         rng = np.random.default_rng(7)
         k[...] = rng.standard_normal(k.shape, dtype=np.float32) * np.float32(w.std)
         v[...] = rng.standard_normal(v.shape, dtype=np.float32) * np.float32(w.std)
         ref.set_batch(ctx, tables)
-        if steps is None or total_budget_s is None or n == 1:
+        if steps is None or total_budget_s is None:
             break
         t_probe = ref.step()
-        if t_probe * (steps + warmup) <= total_budget_s:
+        if t_probe * (steps + warmup) <= total_budget_s or (n == 1 and int(ctx.max()) <= 16):
             break
         ref.close()
-        n = max(1, min(n - 1, int(n * total_budget_s / (t_probe * (steps + warmup)))))
+        f = total_budget_s / (t_probe * (steps + warmup))
+        longest = int(ctx.max())
+        if longest > 16:
+            cap = max(16, min(longest - 16, int(longest * f * 0.9)))
+        else:
+            n = max(1, min(n - 1, int(n * f)))
     try:
         for _ in range(warmup):
             ref.step()
@@ -879,14 +890,15 @@ def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | Non
         ref.close()
     t = sum(times) / len(times)
     sample_bytes = int(ctx.astype(np.int64).sum()) * 2 * w.num_kv_heads * w.head_dim * w.elem_bytes
+    cut = f", contexts cut to their first {cap} tokens" if cap is not None else ""
     return {
         "value": round(sample_bytes / t / 1e9, 3),
         "unit": UNIT,
         "cores": threads,
         "kind": "reference",
         "sample": (f"CacheFlow BatchDecodeEngine::step, CPU build (batch_decode.cpp:33-88,190-240; fp32, "
-                   f"reads K only, no output) on the first {len(ctx)} of {w.num_seqs} sequences of {w.name} "
-                   f"({int(ctx.sum())} tokens), {len(times)} steps of {t*1e3:.1f} ms, {threads} threads; "
+                   f"reads K only, no output) on the first {len(ctx)} of {w.num_seqs} sequences of {w.name}"
+                   f"{cut} ({int(ctx.sum())} tokens), {len(times)} steps of {t*1e3:.1f} ms, {threads} threads; "
                    f"value = that sample's {w.dtype} KV bytes / step time"),
         "tokens_per_s": round(len(ctx) / t, 2),
     }
