@@ -100,6 +100,7 @@ class DecodeEngine:
             self.tmp_out = torch.empty((max_seqs, num_heads, self.parts, self.head_dim), dtype=torch.float32,
                                        device=dev)
         self.launches_per_step = 0
+        self.side = None  # created by the first mixed step
         # Decode steps whose new tokens are exactly one per row, at each row's
         # newest position, append and attend in one launch
         # (paged_attention_append_v1/_v2) instead of reshape_and_cache + attention.
@@ -168,12 +169,26 @@ class DecodeEngine:
 
     def _attend_mixed(self, b, num_seqs, max_context_len, chunks):
         """Decode rows [0, num_decode) with paged attention, the remaining rows
-        as prefill chunks with the multi-query operator."""
+        as prefill chunks with the multi-query operator.  The two launches run
+        concurrently: the prefill (tensor-bound) on the current stream, the
+        decode rows (HBM-bound) on a high-priority side stream forked from it
+        and joined back into it, so the decode CTAs take SMs as the prefill's
+        retire instead of waiting for the whole prefill grid."""
         nd, nc, max_q = chunks
+        cur = torch.cuda.current_stream(self.device)
         if nd:
-            self._attend(b.q[:nd], b.out[:nd], b.tables[:nd], b.ctx[:nd], nd, max_context_len)
+            if self.side is None:
+                self.side = torch.cuda.Stream(self.device, priority=-5)  # clamped to the highest
+                self.fork, self.joined = torch.cuda.Event(), torch.cuda.Event()
+            self.fork.record(cur)
+            self.side.wait_event(self.fork)
         ops.paged_prefill_attention(b.out[nd:num_seqs], b.q[nd:num_seqs], self.k, self.v, b.c_tables[:nc],
                                     b.c_ctx[:nc], b.c_start[: nc + 1], None, max_q)
+        if nd:
+            with torch.cuda.stream(self.side):
+                self._attend(b.q[:nd], b.out[:nd], b.tables[:nd], b.ctx[:nd], nd, max_context_len)
+            self.joined.record(self.side)
+            cur.wait_event(self.joined)
         self.launches_per_step += 1
 
     def attend(self, num_seqs: int, max_context_len: int, chunks=None, new=None) -> None:
