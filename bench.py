@@ -649,7 +649,8 @@ def rebalance_check(full, parts, rank: int, world: int, k_cache, v_cache) -> dic
         "sequences_verified": verified,
         "bitwise_equal": mismatched == 0 and errs == 0,
         "how": ("seeded finishes (rank r loses 0.4*r/(N-1) of its sequences), plan_rebalance to 2 %, "
-                "migrate(): block-copy gather, NCCL send/recv into the receiver's HBM, scatter (rank pairs connected "
+                "migrate(): block-copy gather, NCCL send/recv into the receiver's HBM, scatter, pipelined in 1 GiB "
+                "chunks (rank pairs connected "
                 "beforehand by a 1-element exchange); ms = CUDA events from the first gather to the last scatter "
                 "on each rank, max over ranks (host_ms: the whole call, bookkeeping included); moved sequences' "
                 "attention recomputed on the receiver"),

@@ -142,7 +142,7 @@ def _four_rank_plan(world):
     return pools, moves
 
 
-def _many_peer_worker(rank, world, port, result_dir):
+def _many_peer_worker(rank, world, port, result_dir, chunk_bytes):
     import torch
     import torch.distributed as dist
 
@@ -160,7 +160,8 @@ def _many_peer_worker(rank, world, port, result_dir):
     moved = {s for s, _, _ in moves}
     stay = [s for s in pools[rank].tables if s not in moved]
     before = {s: (k[pools[rank].tables[s]].clone(), v[pools[rank].tables[s]].clone()) for s in stay}
-    stats = sharding.migrate(moves, rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter, timeout_s=60)
+    stats = sharding.migrate(moves, rank, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter, timeout_s=60,
+                             chunk_bytes=chunk_bytes)
     dist.barrier()
     ok = True
     got = 0
@@ -180,16 +181,20 @@ def _many_peer_worker(rank, world, port, result_dir):
     dist.destroy_process_group()
 
 
-def test_block_migration_four_gloo_ranks_many_peers(tmp_path):
+@pytest.mark.parametrize("chunk_bytes", [1 << 30, 3 * 1024])
+def test_block_migration_four_gloo_ranks_many_peers(tmp_path, chunk_bytes):
     """plan_rebalance's moves between four ranks (several senders and
-    receivers, some ranks both) through one migrate() call per rank."""
+    receivers, some ranks both) through one migrate() call per rank: in one
+    transfer group, and in chunks of one block (K and V: 2 KB of 3 KB), so
+    every pair spans many groups of different counts."""
     import torch.multiprocessing as mp
 
     _, moves = _four_rank_plan(4)
     pairs = {(a, b) for _, a, b in moves}
     assert len(moves) >= 3 and len(pairs) >= 2, moves
     port = _free_port()
-    mp.start_processes(_many_peer_worker, args=(4, port, str(tmp_path)), nprocs=4, start_method="spawn")
+    mp.start_processes(_many_peer_worker, args=(4, port, str(tmp_path), chunk_bytes), nprocs=4,
+                       start_method="spawn")
     for r in range(4):
         assert (tmp_path / f"ok{r}").read_text() == "1", r
 
