@@ -803,6 +803,7 @@ def run_ours(args):
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+            line["cpu_port"] = cpu_port_baseline(w)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -902,6 +903,50 @@ def cpu_baseline(w: workloads.Workload, budget_s: float = 15.0, steps: int | Non
                    f"{cut} ({int(ctx.sum())} tokens), {len(times)} steps of {t*1e3:.1f} ms, {threads} threads; "
                    f"value = that sample's {w.dtype} KV bytes / step time"),
         "tokens_per_s": round(len(ctx) / t, 2),
+    }
+
+
+def cpu_port_baseline(w: workloads.Workload, max_seqs: int = 16, max_tokens: int = 2048,
+                      budget_s: float = 4.0) -> dict:
+    """The oracle's C restatement of the decode step (correct softmax
+    attention in f64, one pass per query head over its KV head's blocks, the
+    reference kernel's loop order) on the first `max_seqs` rows of `w`, each
+    context cut to its first `max_tokens` tokens, timed with all host threads
+    (repeated for about `budget_s`) and with one."""
+    import math
+
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(11)
+    code = oracle.BF16 if w.dtype == "bf16" else None
+    ctx, tables, pool = reference_sample(w, min(w.num_seqs, max_seqs), max_tokens)
+    q = workloads.host_values((len(ctx), w.num_heads, w.head_dim), w.dtype, w.std, rng)
+    k = workloads.host_values((pool, w.num_kv_heads, 16, w.head_dim), w.dtype, w.std, rng)
+    v = workloads.host_values((pool, w.num_kv_heads, 16, w.head_dim), w.dtype, w.std, rng)
+    scale = 1.0 / math.sqrt(w.head_dim)
+    times = {}
+    for nt in (threads, 1):
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.paged_attention(q, k, v, tables, ctx, scale, code, num_threads=nt)
+            reps += 1
+            if nt == 1 or time.perf_counter() - t0 > budget_s or reps >= 50:
+                break
+        times[nt] = (time.perf_counter() - t0) / reps
+    kv_bytes = int(ctx.astype(np.int64).sum()) * 2 * w.num_kv_heads * w.head_dim * w.elem_bytes
+    return {
+        "value": round(kv_bytes / times[threads] / 1e9, 3),
+        "value_one_thread": round(kv_bytes / times[1] / 1e9, 3),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"the oracle's C restatement (oracle/cf_oracle.c cfo_paged_attention: f64 softmax attention, "
+                   f"per query head over its KV head's blocks) on the first {len(ctx)} of {w.num_seqs} sequences "
+                   f"of {w.name}, contexts cut to their first {max_tokens} tokens ({int(ctx.sum())} tokens): "
+                   f"{times[threads]*1e3:.1f} ms per step on {threads} threads, {times[1]*1e3:.1f} ms on one; "
+                   f"value = the sample's {w.dtype} KV bytes / step time"),
     }
 
 
