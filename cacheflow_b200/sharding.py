@@ -177,13 +177,40 @@ class MigrationTimeout(MigrationError):
     """The transfers of a migration did not finish before its deadline."""
 
 
+# migrate() calls made by this process: every rank makes the same calls, so
+# the count names one call consistently across ranks.
+_migrate_calls = 0
+
+
 class P2PTransport:
     """Point-to-point transfers through torch.distributed: NCCL send/recv over
-    NVLink between GPUs, gloo between CPU processes.  Every transfer of one
-    migration is posted in a single batch_isend_irecv group."""
+    NVLink between GPUs, gloo between CPU processes, posted as
+    batch_isend_irecv groups."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, store=None):
         self.group = group
+        self.store = store
+
+    def check_peers(self, call: int, peers, timeout_s: float) -> None:
+        """Host-side liveness check before anything is posted: this rank
+        publishes a key for migration call `call` in the process group's
+        store and waits, at most `timeout_s`, for the keys of the peers it
+        exchanges with.  A peer that exited or never reaches the call raises
+        MigrationError while no transfer of the call is on the device."""
+        import datetime
+
+        import torch.distributed as dist
+
+        store = self.store if self.store is not None else dist.distributed_c10d._get_default_store()
+        me = dist.get_rank()
+        store.set(f"cf_migrate/{call}/{me}", "1")
+        keys = [f"cf_migrate/{call}/{p}" for p in peers]
+        try:
+            store.wait(keys, datetime.timedelta(seconds=max(timeout_s, 1e-3)))
+        except Exception as e:  # the store reports the timeout as a RuntimeError (or a subclass)
+            missing = [p for p, k in zip(peers, keys) if not store.check([k])]
+            raise MigrationError(f"migration call {call}: ranks {missing} did not arrive within "
+                                 f"{timeout_s:g} s ({e})") from None
 
     def start(self, sends, recvs) -> list:
         """sends / recvs: lists of (tensor, peer rank).  Returns handles."""
@@ -270,7 +297,10 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
     MigrationTimeout is raised with this rank's bookkeeping unchanged
     (MigrationError, its base, when a transfer fails before the deadline,
     e.g. because the peer exited); scatters already queued have then only
-    written blocks that stay free.  On success every rank applies the moves
+    written blocks that stay free.  Before any of that, the transport's
+    check_peers (if it has one) confirms on the host, through the process
+    group's store, that every peer of this rank reached the same call: a peer
+    that exited between steps raises MigrationError with nothing posted.  On success every rank applies the moves
     to `pools`.  Returns {"blocks_sent", "blocks_received", "bytes_sent",
     "bytes_received", "device_ms", "host_ms", "groups"} for this rank (K and
     V; device_ms: CUDA events on the current stream from the first gather to
@@ -306,6 +336,12 @@ def migrate(moves, rank: int, pools: list[LocalPool], k_cache, v_cache,
                for p in out_peers}
     in_ids = {p: np.fromiter((b for q, s, d in moves if s == p and d == rank for b in dst_ids[q]), np.int64)
               for p in in_peers}
+    # every peer of this call alive (on the host) before anything is posted
+    global _migrate_calls
+    _migrate_calls += 1
+    peers = sorted(set(out_peers) | set(in_peers))
+    if peers and hasattr(transport, "check_peers"):
+        transport.check_peers(_migrate_calls, peers, max(0.0, deadline - time.monotonic()))
     # staging buffers first: their allocation is host work, outside device_ms
     stage_out = {p: (torch.empty((len(i),) + tail, dtype=k_cache.dtype, device=k_cache.device),
                      torch.empty((len(i),) + tail, dtype=k_cache.dtype, device=k_cache.device))

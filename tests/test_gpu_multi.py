@@ -130,8 +130,8 @@ def _worker_both_ways(rank, world, port, result_dir):
 
 
 def test_migration_both_ways_over_nccl(cflib, tmp_path):
-    """Six sequences, three each way, in one migrate() call: one batched NCCL
-    group, deadline-bounded wait, attention bitwise unchanged on both ranks."""
+    """Six sequences, three each way, in one migrate() call: NCCL groups,
+    deadline-bounded waits, attention bitwise unchanged on both ranks."""
     import torch
     import torch.multiprocessing as mp
 
@@ -139,3 +139,59 @@ def test_migration_both_ways_over_nccl(cflib, tmp_path):
         pytest.skip("needs 2 GPUs")
     mp.start_processes(_worker_both_ways, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
     assert (tmp_path / "ok0").read_text() == "1" and (tmp_path / "ok1").read_text() == "1"
+
+
+def _worker_peer_gone(rank, world, port, result_dir):
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from cacheflow_b200 import sharding
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20),
+                            device_id=dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, none of its kernels or collectives in flight
+    ctx = np.array([3000, 700, 5000, 120], np.int64)
+    pools = sharding.shard_workload(ctx, world, pool_factor=3.0, rng=np.random.default_rng(5))
+    nb = max(p.num_blocks for p in pools)
+    k = torch.zeros((nb, 8, 16, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    seq = max(pools[0].tables, key=lambda s: pools[0].lens[s])
+    before = (dict(pools[0].tables), dict(pools[1].tables))
+    t0 = time.monotonic()
+    try:
+        sharding.migrate([(seq, 0, 1)], 0, pools, k, v, timeout_s=3.0)
+        res = "completed"
+    except sharding.MigrationError as e:
+        res = "error" if "did not arrive" in str(e) else "other"
+    torch.cuda.synchronize(dev)  # nothing was posted: the device is idle
+    unchanged = before == (dict(pools[0].tables), dict(pools[1].tables))
+    with open(os.path.join(result_dir, "r0"), "w") as f:
+        f.write(f"{res} {unchanged} {time.monotonic() - t0:.2f}")
+    dist.distributed_c10d._abort_process_group()
+    os._exit(0)
+
+
+def test_migration_to_a_rank_that_left_over_nccl(cflib, tmp_path):
+    """Rank 1 exits between steps; rank 0's migrate() learns it on the host
+    (the process group's store) and raises MigrationError before posting any
+    NCCL operation, its pools unchanged and its GPU idle (NVLS off)."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_worker_peer_gone, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    res, unchanged, secs = (tmp_path / "r0").read_text().split()
+    assert res == "error" and unchanged == "True", (res, unchanged)
+    assert float(secs) < 10.0

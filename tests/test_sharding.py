@@ -199,6 +199,63 @@ def test_block_migration_four_gloo_ranks_many_peers(tmp_path, chunk_bytes):
         assert (tmp_path / f"ok{r}").read_text() == "1", r
 
 
+class _RecordingTransport(sharding.P2PTransport):
+    """Counts the transfer groups it is asked to post."""
+
+    def __init__(self):
+        super().__init__()
+        self.posted = 0
+
+    def start(self, sends, recvs):
+        self.posted += 1
+        return super().start(sends, recvs)
+
+
+def _peer_gone_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.barrier()
+    if rank == 1:
+        os._exit(0)  # leaves between steps: nothing of it is in flight
+    ctx = np.array([300, 50, 700, 20, 400, 90], np.int64)
+    pools = sharding.shard_workload(ctx, world, pool_factor=3.0, rng=np.random.default_rng(5))
+    shape = (max(p.num_blocks for p in pools) + 64, 2, 16, 8)
+    k, v = torch.randn(shape), torch.randn(shape)
+    seq = max(pools[0].tables, key=lambda s: pools[0].lens[s])
+    before = {r: (dict(p.tables), dict(p.lens)) for r, p in enumerate(pools)}
+    tr = _RecordingTransport()
+    t0 = time.monotonic()
+    try:
+        sharding.migrate([(seq, 0, 1)], 0, pools, k, v, gather=_cpu_gather, scatter=_cpu_scatter, transport=tr,
+                         timeout_s=2.0)
+        res = "completed"
+    except sharding.MigrationTimeout:
+        res = "timeout"
+    except sharding.MigrationError as e:
+        res = "error" if "did not arrive" in str(e) else f"other error: {e}"
+    unchanged = all(before[r] == (dict(p.tables), dict(p.lens)) for r, p in enumerate(pools))
+    with open(os.path.join(result_dir, "r0"), "w") as f:
+        f.write(f"{res} {tr.posted} {unchanged} {time.monotonic() - t0:.2f}")
+    os._exit(0)  # no teardown with a peer that is gone
+
+
+def test_migration_to_a_rank_that_left_fails_before_posting(tmp_path):
+    """A peer that exited between steps: migrate() finds it missing in the
+    process group's store, raises MigrationError within its deadline, posts
+    no transfer and leaves the pools as they were."""
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    mp.start_processes(_peer_gone_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    res, posted, unchanged, secs = (tmp_path / "r0").read_text().split()
+    assert res == "error" and posted == "0" and unchanged == "True", (res, posted, unchanged)
+    assert float(secs) < 10.0
+
+
 class _DropSecondSend(sharding.P2PTransport):
     """Posts only the first of its sends: the V slice is lost on the way."""
 
