@@ -26,3 +26,24 @@ def test_reference_arm_prints_one_contract_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_cpu_samples_cut_contexts_not_rows():
+    """The CPU baselines' bounded samples keep their rows (the reference step
+    spreads rows over its threads) and cut each context to its first tokens;
+    the block ids are renumbered into a compact pool."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from cacheflow_b200 import workloads
+
+    w = workloads.make("llama3_70b_sharded")
+    ctx, tables, pool = bench.reference_sample(w, 16, 100)
+    assert len(ctx) == 16 and int(ctx.max()) <= 100 and np.all(ctx == np.minimum(w.context_lens[:16], 100))
+    nblk = (ctx.astype(np.int64) + 15) // 16
+    used = np.concatenate([tables[i, :nblk[i]] for i in range(len(ctx))])
+    assert pool == len(np.unique(used)) and used.min() == 0 and used.max() == pool - 1
+
+    r = bench.cpu_port_baseline(workloads.make("cpu_decode_fp32"), budget_s=0.2)
+    assert r["kind"] == "port" and r["value"] > 0 and r["value_one_thread"] > 0 and r["cores"] >= 1
